@@ -1,0 +1,189 @@
+"""Python host mirror of librocketnpu (B200 build).
+
+ctypes bindings over ``librocketnpu.so`` -- the C-ABI library whose headers
+are ``include/rocket_npu.h`` and ``include/rocket_matmul.h``.  Function names,
+argument meaning and return codes are the reference's (gregordinary/
+rocket-userspace ``include/rocket_matmul.h``); the thin wrappers below only
+convert numpy arrays / torch tensors to pointers.  There is no fallback: if
+the shared library is missing, importing this module raises.
+
+Pointers may be host memory (numpy arrays, CPU tensors) or device memory
+(CUDA tensors on the handle's GPU), exactly as the C entry points accept.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int8, c_int32, c_long, c_size_t, c_uint64, c_void_p
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "librocketnpu.so")
+
+ROCKET_OK = 0
+ROCKET_E_SHAPE = -1
+ROCKET_E_TILING = -2
+ROCKET_E_NOMEM = -3
+ROCKET_E_DEVICE = -4
+ROCKET_E_UNSUPPORTED = -5
+
+# (name, restype, argtypes) for every symbol the public headers declare.
+_P = c_void_p
+_SIGS = [
+    # rocket_npu.h
+    ("rocket_open", c_int, []),
+    ("rocket_close", None, [c_int]),
+    ("rocket_affinity_set_base", None, [c_int]),
+    ("rocket_affinity_get_base", c_int, []),
+    ("rocket_pin_worker", None, [c_int]),
+    ("rocket_num_big_cores", c_int, []),
+    ("rocket_bo_alloc", c_int, [c_int, c_size_t, _P]),
+    ("rocket_bo_free", None, [c_int, _P]),
+    ("rocket_bo_prep", c_int, [c_int, _P, c_int, c_uint64]),
+    ("rocket_bo_fini", c_int, [c_int, _P]),
+    ("rocket_bo_prep_ranges", c_int, [c_int, _P, _P, ctypes.c_uint, c_uint64]),
+    ("rocket_bo_fini_ranges", c_int, [c_int, _P, _P, ctypes.c_uint]),
+    ("rocket_bo_ranges_supported", c_int, []),
+    ("rocket_batched_submit_supported", c_int, []),
+    ("rocket_ppu_done_supported", c_int, []),
+    ("rocket_batch_completion_tracked", c_int, []),
+    ("rocket_busy_poll_set_us", None, [c_long]),
+    ("rocket_submit_matmul", c_int, [c_int, _P, ctypes.c_uint32, _P, ctypes.c_uint32, _P, ctypes.c_uint32, ctypes.c_uint32]),
+    ("rocket_submit_matmul_flags", c_int, [c_int, _P, ctypes.c_uint32, _P, ctypes.c_uint32, _P, ctypes.c_uint32, ctypes.c_uint32]),
+    ("rocket_submit_tasks", c_int, [c_int, _P, ctypes.c_uint32, _P, ctypes.c_uint32, _P, ctypes.c_uint32]),
+    ("rocket_submit_tasks_flags", c_int, [c_int, _P, ctypes.c_uint32, _P, ctypes.c_uint32, _P, ctypes.c_uint32, ctypes.c_uint32]),
+    ("rocket_submit_scratch_size", c_size_t, [ctypes.c_uint32]),
+    ("rocket_submit_tasks_pre", c_int, [c_int, _P, _P, ctypes.c_uint32, _P, ctypes.c_uint32, _P, ctypes.c_uint32, ctypes.c_uint32]),
+    ("rocket_submit_jobs", c_int, [c_int, _P, ctypes.c_uint32]),
+    ("rocket_submit_ioctl_count", c_uint64, []),
+    ("rocket_submit_task_count", c_uint64, []),
+    ("rocket_submit_counters_reset", None, []),
+    # rocket_log.h
+    ("rocket_log_set_callback", None, [_P, _P]),
+    ("rocket_log_set_level", None, [c_int]),
+    ("rocket_log_get_level", c_int, []),
+    # rocket_matmul.h
+    ("rocket_matmul_plan", c_int, [c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_plan_int8", c_int, [c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_plan_int8_gw", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_plan_int4", c_int, [c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_fp16", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_int8", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_int8_groupwise", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, c_int]),
+    ("rocket_matmul_int4", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_int4_ex", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P, c_int]),
+    ("rocket_matmul_int4_groupwise", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, c_int]),
+    ("rocket_matmul_fp16_mt", c_int, [c_int, c_int, c_int, _P, _P, _P, c_int]),
+    ("rocket_ctx_create", _P, [c_int]),
+    ("rocket_ctx_free", None, [_P]),
+    ("rocket_weights_pack", _P, [_P, c_int, c_int, c_int, _P]),
+    ("rocket_weights_free", None, [_P, _P]),
+    ("rocket_matmul_fp16_prepacked", c_int, [_P, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_i8_ctx_create", _P, [c_int]),
+    ("rocket_i8_ctx_free", None, [_P]),
+    ("rocket_i8_weights_pack", _P, [_P, c_int, c_int, c_int, _P]),
+    ("rocket_i8_weights_pack_gw", _P, [_P, c_int, c_int, c_int, _P, c_int]),
+    ("rocket_i8_weights_free", None, [_P, _P]),
+    ("rocket_i8_weights_bytes", c_size_t, [_P]),
+    ("rocket_matmul_int8_prepacked", c_int, [_P, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_int8_prepacked_gw", c_int, [_P, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
+    ("rocket_i4_ctx_create", _P, [c_int]),
+    ("rocket_i4_ctx_free", None, [_P]),
+    ("rocket_i4_weights_pack", _P, [_P, c_int, c_int, c_int, _P]),
+    ("rocket_i4_weights_pack_gw", _P, [_P, c_int, c_int, c_int, _P, c_int]),
+    ("rocket_i4_weights_free", None, [_P, _P]),
+    ("rocket_i4_weights_bytes", c_size_t, [_P]),
+    ("rocket_matmul_int4_prepacked", c_int, [_P, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_int4_prepacked_gw", c_int, [_P, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
+]
+
+EXTRA_SIGS: list = []   # second-tier ops register here (see ops.py)
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"librocketnpu.so not built at {LIB_PATH}: run `make -C rocket-userspace_b200` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, res, args in _SIGS:
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def declared_symbols() -> list[str]:
+    return [n for n, _, _ in _SIGS]
+
+
+# ---------------------------------------------------------------- pointer glue
+def ptr(x) -> int:
+    """Address of a numpy array or torch tensor (contiguous), or 0 for None."""
+    if x is None:
+        return 0
+    if hasattr(x, "data_ptr"):
+        if not x.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+        return x.data_ptr()
+    if hasattr(x, "ctypes"):
+        if not x.flags["C_CONTIGUOUS"]:
+            raise ValueError("array must be C-contiguous")
+        return x.ctypes.data
+    raise TypeError(type(x))
+
+
+class Device:
+    """An open device handle (rocket_open / rocket_close)."""
+
+    def __init__(self):
+        self.fd = lib.rocket_open()
+        if self.fd < 0:
+            raise RuntimeError(f"rocket_open failed ({self.fd})")
+
+    def close(self):
+        if self.fd >= 0:
+            lib.rocket_close(self.fd)
+            self.fd = -1
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    # one-shot entries; return the rocket_status
+    def matmul_fp16(self, M, K, N, A, B, C):
+        return lib.rocket_matmul_fp16(self.fd, M, K, N, ptr(A), ptr(B), ptr(C))
+
+    def matmul_int8(self, M, K, N, A, B, C):
+        return lib.rocket_matmul_int8(self.fd, M, K, N, ptr(A), ptr(B), ptr(C))
+
+    def matmul_int4(self, M, K, N, A, B, C, kt_cap=0):
+        return lib.rocket_matmul_int4_ex(self.fd, M, K, N, ptr(A), ptr(B), ptr(C), kt_cap)
+
+    def matmul_int8_groupwise(self, M, K, N, A, B, a_scale, b_scale, Cf, group):
+        return lib.rocket_matmul_int8_groupwise(self.fd, M, K, N, ptr(A), ptr(B), ptr(a_scale),
+                                                ptr(b_scale), ptr(Cf), group)
+
+    def matmul_int4_groupwise(self, M, K, N, A, B, a_scale, b_scale, Cf, group):
+        return lib.rocket_matmul_int4_groupwise(self.fd, M, K, N, ptr(A), ptr(B), ptr(a_scale),
+                                                ptr(b_scale), ptr(Cf), group)
+
+
+def plan(kind: str, M, K, N, group=None):
+    mt, kt, nt = c_int(), c_int(), c_int()
+    r = ctypes.byref
+    if kind == "fp16":
+        rc = lib.rocket_matmul_plan(M, K, N, r(mt), r(kt), r(nt))
+    elif kind == "int8":
+        rc = lib.rocket_matmul_plan_int8(M, K, N, r(mt), r(kt), r(nt))
+    elif kind == "int8_gw":
+        rc = lib.rocket_matmul_plan_int8_gw(M, K, N, group, r(mt), r(kt), r(nt))
+    elif kind == "int4":
+        rc = lib.rocket_matmul_plan_int4(M, K, N, r(mt), r(kt), r(nt))
+    else:
+        raise ValueError(kind)
+    return rc, (mt.value, kt.value, nt.value)

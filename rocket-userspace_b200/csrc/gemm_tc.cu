@@ -1,0 +1,321 @@
+// gemm_tc.cu -- dense C[M,N] = A[M,K] * B[N,K]^T on the sm_100a tensor cores.
+//
+// This is the kernel behind rocket_matmul_fp16 / rocket_matmul_int8 and their
+// resident and multi-GPU forms (reference src/rocket_matmul.c:975-1105 and
+// :2439-2627 run the same contraction as NPU tile programs with host K-accum).
+//
+// Design (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: 128-byte-swizzled A (128 x 128 B) and B (BN x 128 B)
+//               K-blocks into a STAGES-deep shared-memory ring.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (kind::f16 with fp32
+//               accumulate, or kind::i8 with exact int32 accumulate) into a TMEM
+//               accumulator of 128 lanes x BN columns; two accumulators
+//               alternate so the epilogue of tile i overlaps the MMAs of i+1.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (warp w owns TMEM
+//               lanes 32*(w%4)..+31 = output rows), convert, store to global.
+// Both operands are K-major ("TN"), which is the layout the reference API
+// defines (B is [N,K] row-major), so no transposes are ever made.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <mutex>
+
+#include "rkb_ptx.cuh"
+#include "rkb_tmap.h"
+#include "../src/rkb_kernels.h"
+#include "../../include/rocket_npu.h"
+
+namespace rkb {
+namespace dense {
+
+constexpr int BM = 128;            // UMMA M (cta_group::1)
+constexpr int BK_BYTES = 128;      // one 128-byte swizzle row per K-block
+constexpr int NUM_THREADS = 192;   // 6 warps
+
+template <int BN>
+struct Cfg {
+    static constexpr int A_BYTES = BM * BK_BYTES;
+    static constexpr int B_BYTES = BN * BK_BYTES;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int TMEM_COLS = 2 * BN;   // two accumulators
+    static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+};
+
+struct Args {
+    int M, N, K;
+    int m_tiles, n_tiles, k_blocks;
+    void *C;
+    long ldc;
+    const float *row_scale;
+    const float *col_scale;
+    int *err;
+};
+
+template <int OUT>
+RKB_DEV void store_chunk(const Args &g, int row, int col, const uint32_t (&r)[32]) {
+    // 32 consecutive columns of one output row; N % 8 == 0 so a vector of 8
+    // is either fully inside or fully outside.
+    if (row >= g.M) return;
+    float rs = g.row_scale ? g.row_scale[row] : 1.0f;
+    if (OUT == RKB_OUT_I32) {
+        int32_t *c = static_cast<int32_t *>(g.C) + static_cast<long>(row) * g.ldc + col;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            if (col + 8 * v + 8 <= g.N) {
+                int4 *dst = reinterpret_cast<int4 *>(c + 8 * v);
+                dst[0] = make_int4(r[8 * v + 0], r[8 * v + 1], r[8 * v + 2], r[8 * v + 3]);
+                dst[1] = make_int4(r[8 * v + 4], r[8 * v + 5], r[8 * v + 6], r[8 * v + 7]);
+            }
+        }
+    } else if (OUT == RKB_OUT_F32) {
+        float *c = static_cast<float *>(g.C) + static_cast<long>(row) * g.ldc + col;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            if (col + 8 * v + 8 <= g.N) {
+                float f[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float cs = g.col_scale ? g.col_scale[col + 8 * v + j] : 1.0f;
+                    f[j] = __uint_as_float(r[8 * v + j]) * rs * cs;
+                }
+                float4 *dst = reinterpret_cast<float4 *>(c + 8 * v);
+                dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+                dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+            }
+        }
+    } else {
+        __half *c = static_cast<__half *>(g.C) + static_cast<long>(row) * g.ldc + col;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            if (col + 8 * v + 8 <= g.N) {
+                uint32_t h[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float a = __uint_as_float(r[8 * v + 2 * j]) * rs;
+                    float b = __uint_as_float(r[8 * v + 2 * j + 1]) * rs;
+                    if (g.col_scale) {
+                        a *= g.col_scale[col + 8 * v + 2 * j];
+                        b *= g.col_scale[col + 8 * v + 2 * j + 1];
+                    }
+                    __half2 p = __floats2half2_rn(a, b);
+                    h[j] = *reinterpret_cast<uint32_t *>(&p);
+                }
+                *reinterpret_cast<uint4 *>(c + 8 * v) = make_uint4(h[0], h[1], h[2], h[3]);
+            }
+        }
+    }
+}
+
+template <int KIND, int OUT, int BN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const Args g) {
+    using C = Cfg<BN>;
+    constexpr int STAGES = C::STAGES;
+    constexpr int BK_ELEMS = (KIND == RKB_IN_F16) ? 64 : 128;
+    constexpr int UMMA_K_BYTES = 32;                      // 16 fp16 or 32 int8 per MMA
+    constexpr int K_STEPS = BK_BYTES / UMMA_K_BYTES;      // 4 MMAs per K-block
+    constexpr uint32_t IDESC = (KIND == RKB_IN_F16) ? idesc_f16_f32acc(BM, BN)
+                                                    : idesc_s8_s32acc(BM, BN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
+    const uint32_t smem_base = smem_u32(smem);
+    auto sA = [&](int s) { return smem_base + s * C::STAGE_BYTES; };
+    auto sB = [&](int s) { return smem_base + s * C::STAGE_BYTES + C::A_BYTES; };
+    auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+    auto empty_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+    auto tfull_bar = [&](int b) { return smem_u32(&bars[2 * STAGES + b]); };
+    auto tempty_bar = [&](int b) { return smem_u32(&bars[2 * STAGES + 2 + b]); };
+    const uint32_t drain_bar = smem_u32(&bars[2 * STAGES + 4]);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull_bar(b), 1);
+            mbar_init(tempty_bar(b), 128);
+        }
+        mbar_init(drain_bar, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int num_tiles = g.m_tiles * g.n_tiles;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                const int mt = t % g.m_tiles, nt = t / g.m_tiles;
+                for (int kb = 0; kb < g.k_blocks; ++kb) {
+                    if (!mbar_wait(empty_bar(s), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) { ok = false; break; }
+                    mbar_arrive_expect_tx(full_bar(s), C::STAGE_BYTES);
+                    tma_load_2d(sA(s), &tmA, kb * BK_ELEMS, mt * BM, full_bar(s));
+                    tma_load_2d(sB(s), &tmB, kb * BK_ELEMS, nt * BN, full_bar(s));
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            int it = 0;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+                const int b = it & 1;
+                const uint32_t aph = (it >> 1) & 1;
+                if (!mbar_wait(tempty_bar(b), aph ^ 1, g.err, ERR_WAIT_MMA_ACC)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t dcol = tmem_base + b * BN;
+                for (int kb = 0; kb < g.k_blocks; ++kb) {
+                    if (!mbar_wait(full_bar(s), ph, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t adesc = smem_desc_sw128(sA(s));
+                    const uint64_t bdesc = smem_desc_sw128(sB(s));
+#pragma unroll
+                    for (int k = 0; k < K_STEPS; ++k) {
+                        const uint64_t koff = static_cast<uint64_t>((k * UMMA_K_BYTES) >> 4);
+                        const uint32_t acc = (kb | k) != 0;
+                        if (KIND == RKB_IN_F16) tc_mma_f16(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                        else                    tc_mma_i8(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                    }
+                    tc_commit(empty_bar(s));
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+                if (ok) tc_commit(tfull_bar(b));
+            }
+            if (!ok) {
+                // Error path: let every MMA already issued finish (bounded wait)
+                // before the accumulators are freed.
+                tc_commit(drain_bar);
+                mbar_wait_drain(drain_bar, 0);
+            }
+        }
+    } else {
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        int it = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+            const int b = it & 1;
+            const uint32_t aph = (it >> 1) & 1;
+            if (!mbar_wait(tfull_bar(b), aph, g.err, ERR_WAIT_EPILOGUE)) break;
+            tc_fence_after();
+            const int mt = t % g.m_tiles, nt = t / g.m_tiles;
+            const int row = mt * BM + q * 32 + lane;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(tbase + c, r);
+                tmem_ld_wait();
+                const int col = nt * BN + c;
+                if (col < g.N) store_chunk<OUT>(g, row, col, r);
+            }
+            tc_fence_before();
+            mbar_arrive(tempty_bar(b));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+template <int KIND, int OUT, int BN>
+int launch(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
+    using C = Cfg<BN>;
+    static std::once_flag attr_once[16];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(attr_once[dev & 15], [] {
+        cudaFuncSetAttribute(gemm_kernel<KIND, OUT, BN>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    });
+    const int esize = (KIND == RKB_IN_F16) ? 2 : 1;
+    const CUtensorMapDataType dt =
+        (KIND == RKB_IN_F16) ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    CUtensorMap ta, tb;
+    if (make_tmap_2d(&ta, d->A, dt, esize, d->K, d->M, d->lda, BK_BYTES / esize, BM) ||
+        make_tmap_2d(&tb, d->B, dt, esize, d->K, d->N, d->ldb, BK_BYTES / esize, BN))
+        return ROCKET_E_SHAPE;
+    Args g;
+    g.M = d->M; g.N = d->N; g.K = d->K;
+    g.m_tiles = (d->M + BM - 1) / BM;
+    g.n_tiles = (d->N + BN - 1) / BN;
+    g.k_blocks = (d->K * esize + BK_BYTES - 1) / BK_BYTES;
+    g.C = d->C; g.ldc = d->ldc;
+    g.row_scale = d->row_scale; g.col_scale = d->col_scale;
+    g.err = err;
+    const int tiles = g.m_tiles * g.n_tiles;
+    const int sms = rkb_device_sm_count(dev);
+    const int grid = tiles < sms ? tiles : sms;
+    gemm_kernel<KIND, OUT, BN><<<grid, NUM_THREADS, C::SMEM, stream>>>(ta, tb, g);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        fprintf(stderr, "rkb gemm launch: %s\n", cudaGetErrorString(e));
+        return ROCKET_E_DEVICE;
+    }
+    return 0;
+}
+
+// Tile-width choice: BN=256 unless that leaves most SMs idle for a shape
+// whose tile count would fill the GPU better with BN=128.
+inline int pick_bn(int M, int N) {
+    const int sms = 148;
+    const long t256 = static_cast<long>((M + BM - 1) / BM) * ((N + 255) / 256);
+    if (t256 >= sms) return 256;
+    const long t128 = static_cast<long>((M + BM - 1) / BM) * ((N + 127) / 128);
+    // waves-efficiency of each choice: tiles / (ceil(tiles/sms) * sms)
+    const double e256 = static_cast<double>(t256) / (((t256 + sms - 1) / sms) * sms);
+    const double e128 = static_cast<double>(t128) / (((t128 + sms - 1) / sms) * sms);
+    return (e128 > e256 * 1.15) ? 128 : 256;
+}
+
+}  // namespace dense
+}  // namespace rkb
+
+extern "C" int rkb_gemm_run(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
+    using namespace rkb::dense;
+    if (d->M <= 0 || d->N <= 0 || d->K <= 0) return ROCKET_E_SHAPE;
+    if ((d->N & 7) || (d->ldc & 7)) return ROCKET_E_SHAPE;
+    const int bn = pick_bn(d->M, d->N);
+#define RKB_DISPATCH(KIND, OUT)                                            \
+    return bn == 256 ? launch<KIND, OUT, 256>(d, err, stream)              \
+                     : launch<KIND, OUT, 128>(d, err, stream)
+    if (d->in_kind == RKB_IN_F16) {
+        if (d->out_kind == RKB_OUT_F16) { RKB_DISPATCH(RKB_IN_F16, RKB_OUT_F16); }
+        if (d->out_kind == RKB_OUT_F32) { RKB_DISPATCH(RKB_IN_F16, RKB_OUT_F32); }
+    } else if (d->in_kind == RKB_IN_I8) {
+        if (d->out_kind == RKB_OUT_I32) { RKB_DISPATCH(RKB_IN_I8, RKB_OUT_I32); }
+    }
+#undef RKB_DISPATCH
+    return ROCKET_E_UNSUPPORTED;
+}

@@ -1,0 +1,207 @@
+// rkb_ptx.cuh -- thin inline-PTX wrappers for the sm_100a primitives the
+// kernels of this library use: mbarriers with bounded waits, TMA tensor and
+// bulk loads, tcgen05 TMEM allocation / MMA / commit / loads, and the shared
+// memory matrix descriptors the MMA reads operands through.
+//
+// Every wait on an mbarrier is bounded: after RKB_WAIT_NS of wall time (read
+// from %globaltimer) the waiter records an error code in the caller-supplied
+// error word and gives up, and every other waiter that sees the word set also
+// gives up, so a kernel whose pipeline stalls returns with a status instead of
+// hanging the GPU.
+#pragma once
+#include <stdint.h>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#define RKB_DEV __device__ __forceinline__
+
+#ifndef RKB_WAIT_NS
+#define RKB_WAIT_NS 2000000000ull   // 2 s: legitimate waits here last microseconds
+#endif
+
+namespace rkb {
+
+// Error codes written to the device error word (first writer wins).
+enum : int {
+    ERR_NONE = 0,
+    ERR_WAIT_PRODUCER = 1,   // TMA producer waited too long for a free stage
+    ERR_WAIT_MMA_FULL = 2,   // MMA issuer waited too long for a loaded stage
+    ERR_WAIT_MMA_ACC  = 3,   // MMA issuer waited too long for a drained accumulator
+    ERR_WAIT_EPILOGUE = 4,   // epilogue waited too long for a finished accumulator
+    ERR_WAIT_DEQUANT  = 5,   // dequant warps waited too long for raw weights / a free slot
+    ERR_WAIT_DRAIN    = 6,   // final drain of in-flight MMAs timed out
+};
+
+RKB_DEV uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+RKB_DEV uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---- mbarriers -------------------------------------------------------------
+RKB_DEV void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+RKB_DEV void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+RKB_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase of parity `parity` to complete.  Returns false if
+// the wait expired (error recorded) or another role already recorded an error.
+RKB_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int *err, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        // The error word may live in mapped host memory: poll it (and the
+        // clock) only every 1024 tries so spinning warps do not flood PCIe.
+        if ((i & 1023u) == 0) {
+            if (*reinterpret_cast<volatile int *>(err) != 0) return false;
+            if (global_timer_ns() - t0 > RKB_WAIT_NS) {
+                // plain store: the word may be mapped host memory, where device
+                // atomics are not atomic anyway; any non-zero code is an error
+                *reinterpret_cast<volatile int *>(err) = code;
+                return false;
+            }
+        }
+    }
+}
+// Bounded wait that ignores the error word (used to drain in-flight async work
+// on an error path).  Returns false on expiry.
+RKB_DEV bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (global_timer_ns() - t0 > RKB_WAIT_NS) return false;
+    return true;
+}
+RKB_DEV void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+RKB_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+// ---- TMA ---------------------------------------------------------------------
+// 2D tiled tensor load, no multicast.  c0 is the inner (contiguous) coordinate
+// in elements; callers keep c0 * element size a multiple of 16 bytes.
+RKB_DEV void tma_load_2d(uint32_t dst, const CUtensorMap *tm, int c0, int c1, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
+// Contiguous bulk copy global -> shared (no tensor map).  dst, src 16-byte
+// aligned and bytes a multiple of 16.
+RKB_DEV void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+        : "memory");
+}
+RKB_DEV void prefetch_tmap(const CUtensorMap *tm) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
+// Make generic-proxy writes to shared memory visible to the async proxy (the
+// tensor core reads operands through it).
+RKB_DEV void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- tcgen05 -------------------------------------------------------------------
+RKB_DEV void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(dst_smem), "r"(ncols) : "memory");
+}
+RKB_DEV void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+RKB_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+RKB_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+RKB_DEV void tc_fence_after()  { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Arrive on `bar` once every tcgen05.mma issued so far by this thread completes.
+RKB_DEV void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(bar) : "memory");
+}
+
+// D(tmem) (+)= A(smem desc) * B(smem desc)^T, fp16/bf16 inputs.
+RKB_DEV void tc_mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+        ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accum) : "memory");
+}
+// D(tmem) (+)= A * B^T, signed/unsigned 8-bit inputs, int32 accumulate.
+RKB_DEV void tc_mma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n"
+        ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accum) : "memory");
+}
+
+// Warp-collective load of 32 consecutive 32-bit TMEM columns for the warp's 32
+// lanes (thread i gets lane base+i).
+RKB_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+}
+RKB_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major operand tile stored with the
+// 128-byte swizzle (rows of 128 bytes, 8-row / 1024-byte swizzle atoms, which is
+// what a TMA load with CU_TENSOR_MAP_SWIZZLE_128B writes):
+//   bits  0-13 start address >> 4        bits 16-29 leading byte offset >> 4 (unused: 1)
+//   bits 32-45 stride byte offset >> 4 (1024 B between 8-row groups)
+//   bits 46-47 descriptor version (1 on sm_100)   bits 61-63 layout (2 = SWIZZLE_128B)
+// The tile base must be 1024-byte aligned; stepping K inside the 128-byte row is
+// done by advancing the start address.
+RKB_DEV uint64_t smem_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>(1) << 16;
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
+// Instruction descriptors (kind::f16 and kind::i8), both operands K-major, dense.
+//   bits 4-5 accumulator format (1 = f32, 2 = s32), bits 7-9 / 10-12 A / B format
+//   (f16: 0 = f16, 1 = bf16; i8: 1 = signed), bits 17-22 N >> 3, bits 24-28 M >> 4.
+__host__ __device__ constexpr uint32_t idesc_f16_f32acc(int m, int n) {
+    return (1u << 4) | (0u << 7) | (0u << 10) |
+           (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t idesc_s8_s32acc(int m, int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) |
+           (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+}  // namespace rkb

@@ -1,0 +1,173 @@
+// rkb_util.cu -- small HBM-bound helper kernels around the GEMMs: the resident
+// weight packers (row-major int8 [N,K] -> tiled offset-binary code blocks and
+// fp16 scale blocks), activation pre-scaling for group-wise A scales, and a
+// per-device SM-count cache.  All are one pass over their input with
+// coalesced loads; none is on the timed path of a prepacked call except
+// rkb_prescale_a (M*K bytes in, 2*M*K bytes out).
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include "../src/rkb_kernels.h"
+#include "../../include/rocket_npu.h"
+
+namespace {
+
+constexpr int TILE_N = 256;
+
+__global__ void pack_codes_i8(const int8_t *__restrict__ src, int N, int K, int nkb,
+                              uint8_t *__restrict__ dst, size_t total) {
+    // dst index -> (nt, kb, r, j): block of 256 x 64 bytes
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int j = static_cast<int>(i & 63);
+        const int r = static_cast<int>((i >> 6) & 255);
+        const size_t blk = i >> 14;
+        const int kb = static_cast<int>(blk % nkb);
+        const int nt = static_cast<int>(blk / nkb);
+        const int n = nt * TILE_N + r, k = kb * 64 + j;
+        int8_t v = (n < N && k < K) ? src[static_cast<size_t>(n) * K + k] : 0;
+        dst[i] = static_cast<uint8_t>(v) ^ 0x80u;
+    }
+}
+
+__global__ void pack_codes_i4(const int8_t *__restrict__ src, int N, int K, int nkb,
+                              uint8_t *__restrict__ dst, size_t total) {
+    // block of 256 rows x 32 bytes; byte j holds codes 2j (low) and 2j+1 (high)
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int j = static_cast<int>(i & 31);
+        const int r = static_cast<int>((i >> 5) & 255);
+        const size_t blk = i >> 13;
+        const int kb = static_cast<int>(blk % nkb);
+        const int nt = static_cast<int>(blk / nkb);
+        const int n = nt * TILE_N + r, k = kb * 64 + 2 * j;
+        int v0 = 0, v1 = 0;
+        if (n < N) {
+            const int8_t *row = src + static_cast<size_t>(n) * K;
+            if (k < K) v0 = row[k];
+            if (k + 1 < K) v1 = row[k + 1];
+        }
+        dst[i] = static_cast<uint8_t>(((v0 + 8) & 15) | (((v1 + 8) & 15) << 4));
+    }
+}
+
+__global__ void pack_scales(const float *__restrict__ bs, int N, int K, int group, int nkb,
+                            __half *__restrict__ dst, size_t total) {
+    const int nG = K / group;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int h = static_cast<int>(i & 1);
+        const int r = static_cast<int>((i >> 1) & 255);
+        const size_t blk = i >> 9;
+        const int kb = static_cast<int>(blk % nkb);
+        const int nt = static_cast<int>(blk / nkb);
+        const int n = nt * TILE_N + r, k = kb * 64 + h * 32;
+        float s = 0.0f;
+        if (bs == nullptr) s = 1.0f;
+        else if (n < N && k < K) s = bs[static_cast<size_t>(n) * nG + k / group];
+        dst[i] = __float2half_rn(s);
+    }
+}
+
+__global__ void prescale_a(const int8_t *__restrict__ A, const float *__restrict__ as, int M,
+                           int K, int group, __half *__restrict__ dst) {
+    // 8 elements per thread (K % 32 == 0 so rows split evenly)
+    const size_t total8 = static_cast<size_t>(M) * K / 8;
+    const int nG = as ? K / group : 0;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total8;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t e = i * 8;
+        const int m = static_cast<int>(e / K), k = static_cast<int>(e % K);
+        const uint2 w = *reinterpret_cast<const uint2 *>(A + e);
+        const float s = as ? as[static_cast<size_t>(m) * nG + k / group] : 1.0f;
+        const int8_t *b = reinterpret_cast<const int8_t *>(&w);
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            __half2 p = __floats2half2_rn(static_cast<float>(b[2 * j]) * s,
+                                          static_cast<float>(b[2 * j + 1]) * s);
+            o[j] = *reinterpret_cast<uint32_t *>(&p);
+        }
+        *reinterpret_cast<uint4 *>(dst + e) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+__global__ void gather_row_scale(const float *__restrict__ as, int M, int nG, float *__restrict__ dst) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m < M) dst[m] = as[static_cast<size_t>(m) * nG];
+}
+
+int grid_for(size_t total, int threads) {
+    size_t b = (total + threads - 1) / threads;
+    if (b > 148 * 16) b = 148 * 16;
+    return b < 1 ? 1 : static_cast<int>(b);
+}
+
+int status(cudaError_t e) { return e == cudaSuccess ? 0 : ROCKET_E_DEVICE; }
+
+}  // namespace
+
+extern "C" {
+
+size_t rkb_wpack_codes_bytes(int N, int K, int bits) {
+    const size_t nt = (N + TILE_N - 1) / TILE_N;
+    const size_t nkb = (K + 127) / 128 * 2;
+    return nt * nkb * TILE_N * 64 * bits / 8;
+}
+
+size_t rkb_wpack_scales_bytes(int N, int K) {
+    const size_t nt = (N + TILE_N - 1) / TILE_N;
+    const size_t nkb = (K + 127) / 128 * 2;
+    return nt * nkb * TILE_N * 2 * sizeof(__half);
+}
+
+int rkb_wpack_codes(const int8_t *src, int N, int K, int bits, void *dst, cudaStream_t s) {
+    const int nkb = (K + 127) / 128 * 2;
+    const size_t total = rkb_wpack_codes_bytes(N, K, bits);
+    if (bits == 8)
+        pack_codes_i8<<<grid_for(total, 256), 256, 0, s>>>(src, N, K, nkb, static_cast<uint8_t *>(dst), total);
+    else if (bits == 4)
+        pack_codes_i4<<<grid_for(total, 256), 256, 0, s>>>(src, N, K, nkb, static_cast<uint8_t *>(dst), total);
+    else
+        return ROCKET_E_UNSUPPORTED;
+    return status(cudaGetLastError());
+}
+
+int rkb_wpack_scales(const float *b_scale, int N, int K, int group, void *dst, cudaStream_t s) {
+    const int nkb = (K + 127) / 128 * 2;
+    const size_t total = rkb_wpack_scales_bytes(N, K) / sizeof(__half);
+    pack_scales<<<grid_for(total, 256), 256, 0, s>>>(b_scale, N, K, group, nkb,
+                                                      static_cast<__half *>(dst), total);
+    return status(cudaGetLastError());
+}
+
+int rkb_wpack_unit_scales(int N, int K, void *dst, cudaStream_t s) {
+    return rkb_wpack_scales(nullptr, N, K, 32, dst, s);
+}
+
+int rkb_prescale_a(const int8_t *A, const float *a_scale, int M, int K, int group, void *dst,
+                   cudaStream_t s) {
+    if (K % 8) return ROCKET_E_SHAPE;
+    const size_t total8 = static_cast<size_t>(M) * K / 8;
+    prescale_a<<<grid_for(total8, 256), 256, 0, s>>>(A, a_scale, M, K, group, static_cast<__half *>(dst));
+    return status(cudaGetLastError());
+}
+
+int rkb_gather_row_scale(const float *a_scale, int M, int nG, float *dst, cudaStream_t s) {
+    gather_row_scale<<<(M + 255) / 256, 256, 0, s>>>(a_scale, M, nG, dst);
+    return status(cudaGetLastError());
+}
+
+int rkb_device_sm_count(int dev) {
+    static int cache[64];
+    if (dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+}  // extern "C"

@@ -1,0 +1,82 @@
+/*
+ * rkb_kernels.h -- internal C ABI between the C host library and the CUDA
+ * kernels (the csrc directory).  Plain pointers and sizes only; every function
+ * enqueues on the given stream and returns 0 or a negative rocket_status.
+ * Pointers are device pointers on the current device.
+ */
+#ifndef RKB_KERNELS_H
+#define RKB_KERNELS_H
+
+#include <stdint.h>
+#include <stddef.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum rkb_in_kind  { RKB_IN_F16 = 0, RKB_IN_I8 = 1 };
+enum rkb_out_kind { RKB_OUT_F16 = 0, RKB_OUT_I32 = 1, RKB_OUT_F32 = 2 };
+
+/* Dense C[M,N] = A[M,K] * B[N,K]^T on tcgen05.  Leading dimensions are in
+ * elements; lda/ldb times the element size must be a multiple of 16 bytes and
+ * A/B 16-byte aligned (TMA rules), ldc a multiple of 8 and N % 8 == 0.
+ * row_scale (length M) / col_scale (length N) are optional fp32 factors
+ * applied to each output element in the epilogue (fp16 / fp32 outputs only). */
+typedef struct {
+    int in_kind, out_kind;
+    int M, N, K;
+    const void *A; long lda;
+    const void *B; long ldb;
+    void *C; long ldc;
+    const float *row_scale;
+    const float *col_scale;
+} rkb_gemm_desc;
+
+int rkb_gemm_run(const rkb_gemm_desc *d, int *err_word, cudaStream_t stream);
+
+/* Group-wise / int4 weight GEMM with in-register dequantisation.
+ * Weights are in the resident tiled layout written by rkb_pack_weights:
+ * for each 256-row N tile and each 64-wide K block, a contiguous block of
+ * 256 x 64 codes (int8: 16 KB, int4: 8 KB nibble-packed) followed in a
+ * separate array by 256 x 2 fp16 scales (one per 32-wide K sub-group).
+ * A is int8 [M, K] (or fp16 when a_f16 != 0, already scaled per group).
+ * Output: fp32 or fp16 [M, N] (ldc), times row_scale[m] when given. */
+typedef struct {
+    int M, N, K;
+    int w_bits;               /* 8 or 4 */
+    int a_f16;                /* A is fp16 (pre-scaled) instead of int8 */
+    const void *A; long lda;  /* elements */
+    const void *Wq;           /* tiled codes */
+    const void *Ws;           /* tiled fp16 scales */
+    void *C; long ldc; int out_kind;
+    const float *row_scale;
+} rkb_wgemm_desc;
+
+int rkb_wgemm_run(const rkb_wgemm_desc *d, int *err_word, cudaStream_t stream);
+
+/* Resident-weight packers (device -> device).  src is the row-major int8
+ * weight [N, K] (values in [-8,7] when bits == 4); dst gets the tiled layout
+ * above.  N is padded up to the 256-row tile with zero codes.  Returns bytes
+ * needed when dst == NULL. */
+size_t rkb_wpack_codes_bytes(int N, int K, int bits);
+size_t rkb_wpack_scales_bytes(int N, int K);
+int rkb_wpack_codes(const int8_t *src, int N, int K, int bits, void *dst, cudaStream_t s);
+/* scales: fp32 [N, K/group] -> tiled fp16 [ntile][kblock][256][2]. */
+int rkb_wpack_scales(const float *b_scale, int N, int K, int group, void *dst, cudaStream_t s);
+/* Unit scales (all 1.0) for the per-channel int4 raw path. */
+int rkb_wpack_unit_scales(int N, int K, void *dst, cudaStream_t s);
+/* A int8 [M,K] * a_scale[m, k/group] -> fp16 [M,K] (pre-scaled activations). */
+int rkb_prescale_a(const int8_t *A, const float *a_scale, int M, int K, int group,
+                   void *dst, cudaStream_t s);
+/* Rows of a_scale [M, nG] all constant?  Host-side check result is passed in
+ * by the caller; this only gathers a_scale[m*nG] into a dense [M] vector. */
+int rkb_gather_row_scale(const float *a_scale, int M, int nG, float *dst, cudaStream_t s);
+
+/* Device properties cached per device. */
+int rkb_device_sm_count(int dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RKB_KERNELS_H */

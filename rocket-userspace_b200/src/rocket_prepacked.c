@@ -1,0 +1,494 @@
+/*
+ * rocket_prepacked.c -- resident weights and the multi-GPU N-split.
+ *
+ * Reference: src/rocket_prepacked.c:79-447 (fp16 ctx / weights),
+ * src/rocket_prepacked_int8.c:140-767 (W8A8, per-channel and group-wise),
+ * src/rocket_prepacked_int4.c:98-686 (W4A4) and src/rocket_matmul_mt.c:58-99.
+ *
+ * The reference's worker = one NPU fd driven by one pthread, computing
+ * C[:, n0:n0+nsub] from the full A.  Here a worker = one device handle (one GPU
+ * and its stream); worker t runs on GPU t % ndev.  The slice split is the
+ * reference's (ceil(N / nthreads) rounded up to the dtype's N atom: 16 fp16,
+ * 32 int8, 64 int4).  One host thread drives every worker asynchronously --
+ * stage A into each GPU, launch, copy each slice into C -- and then waits for
+ * all of them, so no pthread per call is needed: a GPU launch does not block
+ * the host the way an NPU fence wait does.
+ *
+ * Weights live on their worker's GPU in the layout the kernel reads directly:
+ *   fp16 / int8 per-channel   row-major slice [nsub, K] (TMA tiles it)
+ *   int8 / int4 group-wise    tiled offset-binary codes (rkb_wpack_codes)
+ *   int4 per-channel          tiled nibble codes, widened to int8 in registers
+ * Because none of these depends on M, the reference's "-2: re-pack for this M"
+ * case never arises; K or N differing from the pack returns ROCKET_E_SHAPE.
+ */
+#include <stdlib.h>
+#include <string.h>
+
+#include "rocket_matmul.h"
+#include "rkb_internal.h"
+
+typedef enum { RW_F16, RW_I8, RW_I8_GW, RW_I4, RW_I4_GW } rw_kind;
+
+typedef struct {
+    int nthreads;
+    int atom;                       /* N alignment of a slice */
+    int fd[RKB_MAX_WORKERS];
+} rkb_rctx;
+
+typedef struct {
+    rw_kind kind;
+    int M, K, N, group, nt;
+    int n0[RKB_MAX_WORKERS], nsub[RKB_MAX_WORKERS];
+    void *dev[RKB_MAX_WORKERS];
+    size_t bytes[RKB_MAX_WORKERS];
+} rkb_rweights;
+
+struct rocket_ctx        { rkb_rctx r; };
+struct rocket_weights    { rkb_rweights w; };
+struct rocket_i8_ctx     { rkb_rctx r; };
+struct rocket_i8_weights { rkb_rweights w; };
+struct rocket_i4_ctx     { rkb_rctx r; };
+struct rocket_i4_weights { rkb_rweights w; };
+
+/* ---- ctx ------------------------------------------------------------------ */
+static int rctx_init(rkb_rctx *c, int nthreads, int atom, const char *who)
+{
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > RKB_MAX_WORKERS) nthreads = RKB_MAX_WORKERS;
+    int ndev = rkb_device_count();
+    if (ndev <= 0) {
+        ROCKET_LOGE("%s: no CUDA device\n", who);
+        return ROCKET_E_DEVICE;
+    }
+    c->nthreads = nthreads;
+    c->atom = atom;
+    const int base = (int)rkb_env_long("ROCKET_DEV", 0);
+    for (int t = 0; t < nthreads; t++) {
+        c->fd[t] = rkb_open_on((base + t) % ndev);
+        if (c->fd[t] < 0) {
+            ROCKET_LOGE("%s: open worker %d failed (%d)\n", who, t, c->fd[t]);
+            for (int u = 0; u < t; u++) rocket_close(c->fd[u]);
+            return ROCKET_E_DEVICE;
+        }
+    }
+    /* let slices copy straight into a peer GPU's output buffer */
+    for (int a = 0; a < nthreads && a < ndev; a++)
+        for (int b = 0; b < nthreads && b < ndev; b++) {
+            if (a == b) continue;
+            int can = 0;
+            cudaDeviceCanAccessPeer(&can, a, b);
+            if (can) {
+                cudaSetDevice(a);
+                cudaDeviceEnablePeerAccess(b, 0);
+                cudaGetLastError();   /* already enabled is fine */
+            }
+        }
+    return 0;
+}
+
+static void rctx_free(rkb_rctx *c)
+{
+    for (int t = 0; t < c->nthreads; t++) rocket_close(c->fd[t]);
+}
+
+/* reference slice rule (src/rocket_prepacked_int8.c:161-165) */
+static int nstep(int N, int nthreads, int atom)
+{
+    int s = ((N + nthreads - 1) / nthreads + atom - 1) / atom * atom;
+    return s < atom ? atom : s;
+}
+
+/* ---- weights ---------------------------------------------------------------- */
+static int rweights_pack(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M, int K, int N,
+                         const void *B, int group, const char *who)
+{
+    memset(w, 0, sizeof *w);
+    w->kind = kind; w->M = M; w->K = K; w->N = N; w->group = group;
+    const int step = nstep(N, c->nthreads, c->atom);
+    const size_t esz = kind == RW_F16 ? 2 : 1;
+    int rc = 0;
+    for (int t = 0; t < c->nthreads; t++) {
+        const int n0 = t * step;
+        const int nsub = n0 >= N ? 0 : (N - n0 < step ? N - n0 : step);
+        w->n0[t] = n0;
+        w->nsub[t] = nsub;
+        if (nsub <= 0) continue;
+        w->nt = t + 1;
+        rkb_handle *h = rkb_get(c->fd[t]);
+        const void *src = (const uint8_t *)B + (size_t)n0 * K * esz;
+        const size_t raw = (size_t)nsub * K * esz;
+        if (kind == RW_F16 || kind == RW_I8) {
+            w->bytes[t] = raw;
+            if (cudaMalloc(&w->dev[t], raw) != cudaSuccess) { rc = ROCKET_E_NOMEM; break; }
+            if (cudaMemcpyAsync(w->dev[t], src, raw, cudaMemcpyDefault, h->stream) != cudaSuccess) {
+                rc = ROCKET_E_DEVICE;
+                break;
+            }
+        } else {
+            const int bits = (kind == RW_I8_GW) ? 8 : 4;
+            w->bytes[t] = rkb_wpack_codes_bytes(nsub, K, bits);
+            const void *dsrc = rkb_stage_in(h, RKB_SCR_B, src, raw);
+            if (!dsrc || cudaMalloc(&w->dev[t], w->bytes[t]) != cudaSuccess) { rc = ROCKET_E_NOMEM; break; }
+            rc = rkb_wpack_codes(dsrc, nsub, K, bits, w->dev[t], h->stream);
+            if (rc) break;
+        }
+        rkb_count(1, 1);
+    }
+    for (int t = 0; t < w->nt; t++) {
+        int fr = rkb_finish(rkb_get(c->fd[t]), who);
+        if (!rc) rc = fr;
+    }
+    if (rc) {
+        cudaGetLastError();
+        for (int t = 0; t < c->nthreads; t++)
+            if (w->dev[t]) { cudaSetDevice(rkb_get(c->fd[t])->device); cudaFree(w->dev[t]); }
+        ROCKET_LOGE("%s: pack failed (%d)\n", who, rc);
+    }
+    return rc;
+}
+
+static void rweights_free(const rkb_rctx *c, rkb_rweights *w)
+{
+    for (int t = 0; t < c->nthreads; t++) {
+        if (!w->dev[t]) continue;
+        rkb_handle *h = rkb_get(c->fd[t]);
+        if (h) cudaStreamSynchronize(h->stream);
+        cudaFree(w->dev[t]);
+        w->dev[t] = NULL;
+    }
+}
+
+static size_t rweights_bytes(const rkb_rweights *w)
+{
+    size_t b = 0;
+    for (int t = 0; t < RKB_MAX_WORKERS; t++) b += w->bytes[t];
+    return b;
+}
+
+/* ---- the fan-out -------------------------------------------------------------- */
+typedef struct {
+    const void *A;        /* [M,K] int8 or fp16 */
+    void *C;              /* [M,N] */
+    const float *a_scale, *b_scale;
+    int out_kind;
+} rrun_args;
+
+static int rrun(const rkb_rctx *c, const rkb_rweights *w, int M, const rrun_args *a,
+                const char *who)
+{
+    const int K = w->K, N = w->N;
+    const size_t esz = w->kind == RW_F16 ? 2 : 1;
+    const size_t osz = a->out_kind == RKB_OUT_F16 ? 2 : 4;
+    const int c_dev = rkb_ptr_device(a->C);
+    int rows_const = 0;
+    if (w->kind == RW_I8_GW || w->kind == RW_I4_GW)
+        rows_const = rkb_ptr_device(a->a_scale) < 0 ? rkb_rows_const(a->a_scale, M, K / w->group) : 0;
+    int rc = 0;
+    for (int t = 0; t < w->nt && !rc; t++) {
+        const int n0 = w->n0[t], nsub = w->nsub[t];
+        if (nsub <= 0) continue;
+        rkb_handle *h = rkb_get(c->fd[t]);
+        const void *dA = rkb_stage_in(h, RKB_SCR_A, a->A, (size_t)M * K * esz);
+        if (!dA) { rc = ROCKET_E_NOMEM; break; }
+        /* write straight into C when it lives on this GPU, else into scratch */
+        uint8_t *cslice = (uint8_t *)a->C + (size_t)n0 * osz;
+        const int direct = (c_dev == h->device) && (((uintptr_t)cslice & 15) == 0);
+        void *dC = direct ? (void *)cslice : rkb_scratch(h, RKB_SCR_C, (size_t)M * nsub * osz);
+        const long ldc = direct ? N : nsub;
+        if (!dC) { rc = ROCKET_E_NOMEM; break; }
+        switch (w->kind) {
+        case RW_F16:
+            rc = rkb_dense_on(h, RKB_IN_F16, RKB_OUT_F16, M, nsub, K, dA, K, w->dev[t], K, dC, ldc);
+            break;
+        case RW_I8:
+            rc = rkb_dense_on(h, RKB_IN_I8, RKB_OUT_I32, M, nsub, K, dA, K, w->dev[t], K, dC, ldc);
+            break;
+        case RW_I4: {
+            rkb_wgemm_desc d;
+            memset(&d, 0, sizeof d);
+            d.M = M; d.N = nsub; d.K = K; d.w_bits = 4; d.a_f16 = 0;
+            d.A = dA; d.lda = K; d.Wq = w->dev[t]; d.Ws = NULL;
+            d.C = dC; d.ldc = ldc; d.out_kind = RKB_OUT_I32;
+            rkb_count(0, 1);
+            rc = rkb_wgemm_run(&d, h->err_dev, h->stream);
+            break;
+        }
+        case RW_I8_GW:
+        case RW_I4_GW:
+            rc = rkb_gw_on(h, M, nsub, K, w->group, w->kind == RW_I8_GW ? 8 : 4, dA, a->a_scale,
+                           rows_const, w->dev[t], a->b_scale + (size_t)n0 * (K / w->group), dC, ldc,
+                           a->out_kind);
+            break;
+        }
+        if (!rc && !direct) {
+            if (cudaMemcpy2DAsync(cslice, (size_t)N * osz, dC, (size_t)nsub * osz, (size_t)nsub * osz,
+                                  (size_t)M, cudaMemcpyDefault, h->stream) != cudaSuccess) {
+                ROCKET_LOGE("%s: slice copy failed: %s\n", who, cudaGetErrorString(cudaGetLastError()));
+                rc = ROCKET_E_DEVICE;
+            }
+        }
+        rkb_count(1, 0);
+    }
+    for (int t = 0; t < w->nt; t++) {
+        if (w->nsub[t] <= 0) continue;
+        int fr = rkb_finish(rkb_get(c->fd[t]), who);
+        if (!rc) rc = fr;
+    }
+    return rc;
+}
+
+static int resolve(const rkb_rweights *w, int M, int K, int N, const char *who)
+{
+    if (M <= 0 || M % 4) {
+        ROCKET_LOGE("%s: M=%d must be a positive multiple of 4 -- pad rows caller-side\n", who, M);
+        return ROCKET_E_SHAPE;
+    }
+    if (K != w->K || N != w->N) {
+        ROCKET_LOGE("%s: shape K=%d N=%d != packed %d/%d\n", who, K, N, w->K, w->N);
+        return ROCKET_E_SHAPE;
+    }
+    return 0;
+}
+
+/* ---- fp16 ----------------------------------------------------------------------- */
+rocket_ctx *rocket_ctx_create(int nthreads)
+{
+    rocket_ctx *c = calloc(1, sizeof *c);
+    if (!c) return NULL;
+    if (rctx_init(&c->r, nthreads, 16, "rocket_ctx_create")) { free(c); return NULL; }
+    return c;
+}
+
+void rocket_ctx_free(rocket_ctx *ctx)
+{
+    if (!ctx) return;
+    rctx_free(&ctx->r);
+    free(ctx);
+}
+
+rocket_weights *rocket_weights_pack(rocket_ctx *ctx, int M, int K, int N, const _Float16 *B)
+{
+    if (!ctx || !B) return NULL;
+    if (rocket_matmul_plan(M, K, N, NULL, NULL, NULL) < 0 || M % 4) {
+        ROCKET_LOGE("rocket_weights_pack: bad shape M=%d K=%d N=%d\n", M, K, N);
+        return NULL;
+    }
+    rocket_weights *w = calloc(1, sizeof *w);
+    if (!w) return NULL;
+    if (rweights_pack(&ctx->r, &w->w, RW_F16, M, K, N, B, 0, "rocket_weights_pack")) { free(w); return NULL; }
+    return w;
+}
+
+void rocket_weights_free(rocket_ctx *ctx, rocket_weights *w)
+{
+    if (!ctx || !w) return;
+    rweights_free(&ctx->r, &w->w);
+    free(w);
+}
+
+int rocket_matmul_fp16_prepacked(rocket_ctx *ctx, int M, int K, int N, const _Float16 *A,
+                                 _Float16 *C, rocket_weights *w)
+{
+    if (!ctx || !w || !A || !C) return ROCKET_E_SHAPE;
+    int rc = resolve(&w->w, M, K, N, "rocket_matmul_fp16_prepacked");
+    if (rc) return rc;
+    rrun_args a = { A, C, NULL, NULL, RKB_OUT_F16 };
+    return rrun(&ctx->r, &w->w, M, &a, "rocket_matmul_fp16_prepacked");
+}
+
+int rocket_matmul_fp16_mt(int M, int K, int N, const _Float16 *A, const _Float16 *B, _Float16 *C,
+                          int nthreads)
+{
+    if (rocket_matmul_plan(M, K, N, NULL, NULL, NULL) < 0 || !A || !B || !C) return ROCKET_E_SHAPE;
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > RKB_MAX_WORKERS) nthreads = RKB_MAX_WORKERS;
+    rkb_rctx c;
+    if (rctx_init(&c, nthreads, 16, "rocket_matmul_fp16_mt")) return ROCKET_E_DEVICE;
+    rkb_rweights w;
+    int rc = rweights_pack(&c, &w, RW_F16, M, K, N, B, 0, "rocket_matmul_fp16_mt");
+    if (!rc) {
+        rrun_args a = { A, C, NULL, NULL, RKB_OUT_F16 };
+        rc = rrun(&c, &w, M, &a, "rocket_matmul_fp16_mt");
+        rweights_free(&c, &w);
+    }
+    rctx_free(&c);
+    return rc;
+}
+
+/* ---- int8 ------------------------------------------------------------------------ */
+rocket_i8_ctx *rocket_i8_ctx_create(int nthreads)
+{
+    rocket_i8_ctx *c = calloc(1, sizeof *c);
+    if (!c) return NULL;
+    if (rctx_init(&c->r, nthreads, 32, "rocket_i8_ctx_create")) { free(c); return NULL; }
+    return c;
+}
+
+void rocket_i8_ctx_free(rocket_i8_ctx *ctx)
+{
+    if (!ctx) return;
+    rctx_free(&ctx->r);
+    free(ctx);
+}
+
+static int i8_shape_ok(const char *who, int M, int K, int N)
+{
+    if (M <= 0 || M % 4 || K <= 0 || K % 32 || N <= 0 || N % 32) {
+        ROCKET_LOGE("%s: bad shape M=%d K=%d N=%d (need M%%4, K%%32, N%%32)\n", who, M, K, N);
+        return 0;
+    }
+    return 1;
+}
+
+rocket_i8_weights *rocket_i8_weights_pack(rocket_i8_ctx *ctx, int M, int K, int N, const int8_t *B)
+{
+    if (!ctx || !B || !i8_shape_ok("rocket_i8_weights_pack", M, K, N)) return NULL;
+    rocket_i8_weights *w = calloc(1, sizeof *w);
+    if (!w) return NULL;
+    if (rweights_pack(&ctx->r, &w->w, RW_I8, M, K, N, B, 0, "rocket_i8_weights_pack")) { free(w); return NULL; }
+    return w;
+}
+
+rocket_i8_weights *rocket_i8_weights_pack_gw(rocket_i8_ctx *ctx, int M, int K, int N,
+                                             const int8_t *B, int group)
+{
+    if (!ctx || !B || !i8_shape_ok("rocket_i8_weights_pack_gw", M, K, N)) return NULL;
+    if (group < 32 || group % 32 || K % group) {
+        ROCKET_LOGE("rocket_i8_weights_pack_gw: bad group=%d (need >=32, %%32, |K) K=%d\n", group, K);
+        return NULL;
+    }
+    rocket_i8_weights *w = calloc(1, sizeof *w);
+    if (!w) return NULL;
+    if (rweights_pack(&ctx->r, &w->w, RW_I8_GW, M, K, N, B, group, "rocket_i8_weights_pack_gw")) {
+        free(w);
+        return NULL;
+    }
+    return w;
+}
+
+void rocket_i8_weights_free(rocket_i8_ctx *ctx, rocket_i8_weights *w)
+{
+    if (!ctx || !w) return;
+    rweights_free(&ctx->r, &w->w);
+    free(w);
+}
+
+size_t rocket_i8_weights_bytes(const rocket_i8_weights *w) { return w ? rweights_bytes(&w->w) : 0; }
+
+int rocket_matmul_int8_prepacked(rocket_i8_ctx *ctx, int M, int K, int N, const int8_t *A,
+                                 int32_t *C, rocket_i8_weights *w)
+{
+    if (!ctx || !w || !A || !C) return ROCKET_E_SHAPE;
+    if (w->w.kind != RW_I8) {
+        ROCKET_LOGE("rocket_matmul_int8_prepacked: weight is group-wise -- use rocket_matmul_int8_prepacked_gw\n");
+        return ROCKET_E_SHAPE;
+    }
+    int rc = resolve(&w->w, M, K, N, "rocket_matmul_int8_prepacked");
+    if (rc) return rc;
+    rrun_args a = { A, C, NULL, NULL, RKB_OUT_I32 };
+    return rrun(&ctx->r, &w->w, M, &a, "rocket_matmul_int8_prepacked");
+}
+
+int rocket_matmul_int8_prepacked_gw(rocket_i8_ctx *ctx, int M, int K, int N, const int8_t *A,
+                                    const float *a_scale, const float *b_scale, float *Cf,
+                                    rocket_i8_weights *w)
+{
+    if (!ctx || !w || !A || !a_scale || !b_scale || !Cf) return ROCKET_E_SHAPE;
+    if (w->w.kind != RW_I8_GW) {
+        ROCKET_LOGE("rocket_matmul_int8_prepacked_gw: weight is per-channel -- use rocket_matmul_int8_prepacked\n");
+        return ROCKET_E_SHAPE;
+    }
+    int rc = resolve(&w->w, M, K, N, "rocket_matmul_int8_prepacked_gw");
+    if (rc) return rc;
+    rrun_args a = { A, Cf, a_scale, b_scale, RKB_OUT_F32 };
+    return rrun(&ctx->r, &w->w, M, &a, "rocket_matmul_int8_prepacked_gw");
+}
+
+/* ---- int4 ------------------------------------------------------------------------ */
+rocket_i4_ctx *rocket_i4_ctx_create(int nthreads)
+{
+    rocket_i4_ctx *c = calloc(1, sizeof *c);
+    if (!c) return NULL;
+    if (rctx_init(&c->r, nthreads, 64, "rocket_i4_ctx_create")) { free(c); return NULL; }
+    return c;
+}
+
+void rocket_i4_ctx_free(rocket_i4_ctx *ctx)
+{
+    if (!ctx) return;
+    rctx_free(&ctx->r);
+    free(ctx);
+}
+
+static int i4_shape_ok(const char *who, int M, int K, int N)
+{
+    if (M <= 0 || M % 4 || K <= 0 || K % 32 || N <= 0 || N % 64) {
+        ROCKET_LOGE("%s: bad shape M=%d K=%d N=%d (need M%%4, K%%32, N%%64)\n", who, M, K, N);
+        return 0;
+    }
+    return 1;
+}
+
+rocket_i4_weights *rocket_i4_weights_pack(rocket_i4_ctx *ctx, int M, int K, int N, const int8_t *B)
+{
+    if (!ctx || !B || !i4_shape_ok("rocket_i4_weights_pack", M, K, N)) return NULL;
+    rocket_i4_weights *w = calloc(1, sizeof *w);
+    if (!w) return NULL;
+    if (rweights_pack(&ctx->r, &w->w, RW_I4, M, K, N, B, 0, "rocket_i4_weights_pack")) { free(w); return NULL; }
+    return w;
+}
+
+rocket_i4_weights *rocket_i4_weights_pack_gw(rocket_i4_ctx *ctx, int M, int K, int N,
+                                             const int8_t *B, int group)
+{
+    if (!ctx || !B || !i4_shape_ok("rocket_i4_weights_pack_gw", M, K, N)) return NULL;
+    if (group < 32 || group % 32 || K % group || 49 * group >= 32767) {
+        ROCKET_LOGE("rocket_i4_weights_pack_gw: bad group=%d (need %%32, |K, 49*group<32767)\n", group);
+        return NULL;
+    }
+    rocket_i4_weights *w = calloc(1, sizeof *w);
+    if (!w) return NULL;
+    if (rweights_pack(&ctx->r, &w->w, RW_I4_GW, M, K, N, B, group, "rocket_i4_weights_pack_gw")) {
+        free(w);
+        return NULL;
+    }
+    return w;
+}
+
+void rocket_i4_weights_free(rocket_i4_ctx *ctx, rocket_i4_weights *w)
+{
+    if (!ctx || !w) return;
+    rweights_free(&ctx->r, &w->w);
+    free(w);
+}
+
+size_t rocket_i4_weights_bytes(const rocket_i4_weights *w) { return w ? rweights_bytes(&w->w) : 0; }
+
+int rocket_matmul_int4_prepacked(rocket_i4_ctx *ctx, int M, int K, int N, const int8_t *A,
+                                 int32_t *C, rocket_i4_weights *w)
+{
+    if (!ctx || !w || !A || !C) return ROCKET_E_SHAPE;
+    if (w->w.kind != RW_I4) {
+        ROCKET_LOGE("rocket_matmul_int4_prepacked: weight is group-wise -- use rocket_matmul_int4_prepacked_gw\n");
+        return ROCKET_E_SHAPE;
+    }
+    int rc = resolve(&w->w, M, K, N, "rocket_matmul_int4_prepacked");
+    if (rc) return rc;
+    rrun_args a = { A, C, NULL, NULL, RKB_OUT_I32 };
+    return rrun(&ctx->r, &w->w, M, &a, "rocket_matmul_int4_prepacked");
+}
+
+int rocket_matmul_int4_prepacked_gw(rocket_i4_ctx *ctx, int M, int K, int N, const int8_t *A,
+                                    const float *a_scale, const float *b_scale, float *Cf,
+                                    rocket_i4_weights *w)
+{
+    if (!ctx || !w || !A || !a_scale || !b_scale || !Cf) return ROCKET_E_SHAPE;
+    if (w->w.kind != RW_I4_GW) {
+        ROCKET_LOGE("rocket_matmul_int4_prepacked_gw: weight is per-channel -- use rocket_matmul_int4_prepacked\n");
+        return ROCKET_E_SHAPE;
+    }
+    int rc = resolve(&w->w, M, K, N, "rocket_matmul_int4_prepacked_gw");
+    if (rc) return rc;
+    rrun_args a = { A, Cf, a_scale, b_scale, RKB_OUT_F32 };
+    return rrun(&ctx->r, &w->w, M, &a, "rocket_matmul_int4_prepacked_gw");
+}
