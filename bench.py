@@ -1,0 +1,470 @@
+#!/usr/bin/env python
+"""Benchmark of librocketnpu's matmul hot path on B200.
+
+Headline workload: the 12B-class prefill GEMM set with
+int8 per-output-channel weights, M = 4096 tokens:
+    QKV     K=3840  N=5888
+    O-proj  K=3840  N=3840
+    gate+up K=3840  N=30720
+    down    K=15360 N=3840
+1755.57 GOP per set.  One step = the four GEMMs through the reference API
+(rocket_matmul_int8_prepacked on a resident rocket_i8_weights), raw int32
+outputs, bit-exact to the reference's host int64 sum.
+
+Multi-GPU (torchrun): every weight is N-sharded across the ranks (the
+reference's worker N-split), each rank holds its column slice and the full A,
+and computes its slice with no collective; total work is fixed, so scaling is
+"strong".  The NCCL all-gather of the outputs (only needed when a caller wants
+the full output on one rank) is timed separately and reported, not included.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0).  See DESIGN.md for the roofline arithmetic.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+M_TOK = 4096
+GEMMS = [("qkv", 3840, 5888), ("o_proj", 3840, 3840), ("gate_up", 3840, 30720), ("down", 15360, 3840)]
+SET_OPS = sum(2.0 * M_TOK * k * n for _, k, n in GEMMS)          # 1.75557e12
+METRIC = "int8 TOPS at 12B-prefill GEMM set (config 5), % of B200 dense int8 peak"
+WORKLOAD = "12B prefill int8 GEMM set M=4096: QKV 3840x5888, O 3840x3840, gate+up 3840x30720, down 15360x3840"
+NOMINAL_INT8_TOPS = 4500.0
+NOMINAL_F16_TFLOPS = 2250.0
+
+
+def load_pkg():
+    """Import rocket-userspace_b200/ (its directory name is not an identifier)."""
+    import importlib.util
+    if "rocket_userspace_b200" in sys.modules:
+        return sys.modules["rocket_userspace_b200"]
+    pkg = os.path.join(REPO, "rocket-userspace_b200")
+    spec = importlib.util.spec_from_file_location("rocket_userspace_b200", os.path.join(pkg, "__init__.py"),
+                                                  submodule_search_locations=[pkg])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["rocket_userspace_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def shard(n, world, rank, atom=32):
+    step = -(-n // world)
+    step = -(-step // atom) * atom
+    n0 = rank * step
+    return n0, max(0, min(step, n - n0))
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, idx):
+        self.idx = idx
+        self.proc = None
+
+    def start(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_baseline(seconds=10.0):
+    """The reference's host matmul (int64-accumulate loop, restated in the
+    oracle and pinned by the reference's gates) on this host's cores, over a
+    bounded sample of gate+up rows; TOPS = ops done / time."""
+    import numpy as np
+    import oracle
+    cores = os.cpu_count() or 1
+    K, N = 3840, 30720
+    A = oracle.uniform_i8(1, -127, 127, (1024, K))
+    B = oracle.uniform_i8(2, -127, 127, (N, K))
+    rows, t0 = 0, time.perf_counter()
+    chunk = max(cores, 8)
+    while time.perf_counter() - t0 < seconds and rows + chunk <= 1024:
+        oracle.matmul_int8(A, B, rows=(rows, rows + chunk), nthreads=cores)
+        rows += chunk
+    dt = time.perf_counter() - t0
+    tops = 2.0 * rows * K * N / dt / 1e12
+    return {"value": tops, "unit": "TOPS", "cores": cores, "kind": "port",
+            "sample": f"{rows} rows of the gate+up GEMM (K=3840, N=30720) in {dt:.1f}s, "
+                      "int64-accumulate host loop of tests/matmul_int8_tiled_rocket.c:77-83 "
+                      "(oracle/oracle.c orc_matmul_int8, -O2), rows split across cores"}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    steps_per = max(1.0, 60.0 / max(args.steps + args.warmup, 1))
+    base = cpu_baseline(seconds=min(20.0, steps_per))
+    line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "TOPS",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": SET_OPS / (base["value"] * 1e12) * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "sampled": True},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference's own host matmul (its gates' int64 loop) on the host cores; the reference "
+                    "library's matmul needs an RK3588 NPU, which this box does not have"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- our arm
+def main_ours(args):
+    import ctypes
+    import torch
+    rank, world, local = dist_env()
+    os.environ["ROCKET_DEV"] = str(local)
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    rkb = load_pkg()
+    L = rkb.lib
+    peaks, peak_src = load_peaks()
+
+    ctx = L.rocket_i8_ctx_create(1)
+    assert ctx, "rocket_i8_ctx_create failed"
+    fd = L.rocket_b200_ctx_fd(ctx, 0)
+    lib_stream = torch.cuda.ExternalStream(L.rocket_b200_stream(fd), device=torch.device("cuda", local))
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1234 + rank)
+    A1 = torch.randint(-127, 128, (M_TOK, 3840), dtype=torch.int8, device="cuda", generator=g)
+    A2 = torch.randint(-127, 128, (M_TOK, 15360), dtype=torch.int8, device="cuda", generator=g)
+    layers = []
+    my_ops = 0.0
+    for name, K, N in GEMMS:
+        n0, ns = shard(N, world, rank)
+        W = torch.randint(-127, 128, (ns, K), dtype=torch.int8, device="cuda", generator=g)
+        w = L.rocket_i8_weights_pack(ctx, M_TOK, K, ns, W.data_ptr())
+        assert w, f"pack {name}"
+        del W
+        C = torch.empty((M_TOK, ns), dtype=torch.int32, device="cuda")
+        A = A1 if K == 3840 else A2
+        layers.append((name, K, ns, w, A, C))
+        my_ops += 2.0 * M_TOK * K * ns
+    torch.cuda.synchronize()
+
+    def step(As=None, Cs=None):
+        for i, (name, K, ns, w, A, C) in enumerate(layers):
+            a = A if As is None else As[i]
+            c = C if Cs is None else Cs[i]
+            rc = L.rocket_matmul_int8_prepacked(ctx, M_TOK, K, ns, a.data_ptr(), c.data_ptr(), w)
+            if rc != 0:
+                raise RuntimeError(f"{name}: rc={rc}")
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timed region
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    L.rocket_b200_profile_reset()
+    L.rocket_b200_profile_enable(1)
+    L.rocket_submit_counters_reset()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(lib_stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(lib_stream)
+    torch.cuda.synchronize()
+    barrier()
+    L.rocket_b200_profile_enable(0)
+    launches = int(L.rocket_submit_task_count())
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms)
+    value = SET_OPS * args.steps / (ms_max / 1e3) / 1e12
+    prof = rkb.profile_snapshot()
+    n_i8, ms_i8 = prof.get("gemm_i8_tcgen05", (0, 0.0))
+
+    # roofline of the dominant kernel (the int8 GEMM), per launch
+    ops_per_launch = my_ops / len(GEMMS)
+    avg_launch_ms = ms_i8 / max(n_i8, 1)
+    achieved = ops_per_launch / (avg_launch_ms / 1e3) / 1e12
+    derived_peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": derived_peak, "unit": "TOPS",
+                "frac": achieved / derived_peak, "traffic": None,
+                "peak_source": f"2 x {peak_src} bf16 burst ({peaks.get('bf16_tflops')} TF/s): "
+                               "B200 dense int8 rate is twice its bf16 rate; no int8 figure in "
+                               "MEASURED_PEAKS.json",
+                "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
+                "kernel": "gemm_i8_tcgen05", "launches": n_i8,
+                "avg_launch_us": avg_launch_ms * 1e3,
+                "kernel_share_of_step": ms_i8 / ms if ms > 0 else None}
+    traffic_file = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(traffic_file):
+        roofline["traffic"] = json.load(open(traffic_file)).get("gemm_i8_config5_avg_launch_bytes")
+
+    # ---- all-gather of the sharded outputs (reported, not in value)
+    gather = None
+    if world > 1:
+        import torch.distributed as dist
+        bufs = []
+        for name, K, ns, w, A, C in layers:
+            n0, nmax = shard(dict((a, b) for a, _, b in GEMMS)[name], world, 0)
+            src = torch.zeros((M_TOK, nmax), dtype=torch.int32, device="cuda")
+            src[:, :ns] = C
+            bufs.append((src, torch.empty((world, M_TOK, nmax), dtype=torch.int32, device="cuda")))
+        for src, dst in bufs:
+            dist.all_gather_into_tensor(dst, src)
+        torch.cuda.synchronize()
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(3):
+            for src, dst in bufs:
+                dist.all_gather_into_tensor(dst, src)
+        g1.record()
+        torch.cuda.synchronize()
+        gms = max_over_ranks(g0.elapsed_time(g1) / 3)
+        gather = {"allgather_ms_per_step": gms, "collective": "nccl all_gather_into_tensor",
+                  "value_with_gather": SET_OPS / ((ms_max / args.steps + gms) / 1e3) / 1e12}
+
+    # ---- end to end through the API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        hA = [torch.empty_like(A, device="cpu").pin_memory() for (_, _, _, _, A, _) in layers]
+        for h, (_, _, _, _, A, _) in zip(hA, layers):
+            h.copy_(A.cpu())
+        hC = [torch.empty(C.shape, dtype=torch.int32).pin_memory() for (_, _, _, _, _, C) in layers]
+        e2e_steps = max(1, min(args.steps, 20))
+        step(hA, hC)
+        torch.cuda.synchronize()
+        barrier()
+        x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x0.record(lib_stream)
+        for _ in range(e2e_steps):
+            step(hA, hC)
+        x1.record(lib_stream)
+        torch.cuda.synchronize()
+        ems = max_over_ranks(x0.elapsed_time(x1))
+        ok = all(torch.equal(hC[i], layers[i][5].cpu()) for i in range(len(layers)))
+        e2e = {"value": SET_OPS * e2e_steps / (ems / 1e3) / 1e12, "unit": "TOPS",
+               "h2d_bytes_per_step": int(sum(h.numel() for h in hA)) * world,
+               "d2h_bytes_per_step": int(sum(h.numel() * 4 for h in hC)) * world,
+               "steps": e2e_steps, "host_result_matches_device": ok,
+               "path": "rocket_matmul_int8_prepacked with pinned host A and C (H2D + D2H inside each call)"}
+
+    # ---- other configs (rank 0, N=1 only)
+    others = None
+    if world == 1 and not args.no_extra:
+        others = other_configs(rkb, torch, peaks, derived_peak)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(seconds=10.0)
+
+    for name, K, ns, w, A, C in layers:
+        L.rocket_i8_weights_free(ctx, w)
+    L.rocket_i8_ctx_free(ctx)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8 (s8 x s8 -> s32, exact)",
+                "data": "synthetic: int8 uniform [-127,127], seeded",
+                "config": {"workload": WORKLOAD, "M": M_TOK, "ops_per_step": SET_OPS,
+                           "parallelism": f"N-shard x{world}", "l2": "working set per step ~1 GB > 126 MB L2 (no flush needed)",
+                           "api": "rocket_matmul_int8_prepacked, device-resident operands"},
+                "frac_of_derived_int8_peak": value / derived_peak,
+                "roofline": roofline, "clocks": clk, "gpu_launches": launches,
+                "e2e": e2e, "cpu_baseline": cpu, "gather": gather, "other_configs": others}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def other_configs(rkb, torch, peaks, derived_i8_peak):
+    """fp16 (config 2), W4A8 group-wise (config 3) and int8 latency (config 1)."""
+    L = rkb.lib
+    out = {}
+    dev = rkb.Device()
+    stream = torch.cuda.ExternalStream(L.rocket_b200_stream(dev.fd))
+
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    # config 2: fp16 512x4096x4096
+    M, K, N = 512, 4096, 4096
+    A = (torch.randn((M, K), device="cuda") / K ** 0.5).half()
+    B = (torch.randn((N, K), device="cuda") / K ** 0.5).half()
+    C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    ms = timed(lambda: dev.matmul_fp16(M, K, N, A, B, C), 50)
+    ref = torch.matmul(A, B.t())
+    t = timed(lambda: torch.matmul(A, B.t()), 50)
+    out["config2_fp16"] = {"tflops": 2 * M * N * K / ms / 1e9, "ms": ms,
+                           "frac_of_measured_bf16": 2 * M * N * K / ms / 1e9 / peaks["bf16_tflops"],
+                           "torch_cublas_tflops": 2 * M * N * K / t / 1e9,
+                           "rel_fro_vs_cublas": float((C.float() - ref.float()).norm() / ref.float().norm())}
+    # large fp16 for the kernel's steady-state rate
+    M2 = 4096
+    A2 = torch.randn((M2, K), device="cuda").half()
+    C2 = torch.empty((M2, N), dtype=torch.float16, device="cuda")
+    ms2 = timed(lambda: dev.matmul_fp16(M2, K, N, A2, B, C2), 30)
+    out["fp16_4096x4096x4096"] = {"tflops": 2 * M2 * N * K / ms2 / 1e9,
+                                  "frac_of_measured_bf16": 2 * M2 * N * K / ms2 / 1e9 / peaks["bf16_tflops"]}
+    del A2, C2
+
+    # config 3: W4A8 group-wise resident 2048x3840x15360, group 32
+    M, K, N, gsz = 2048, 3840, 15360, 32
+    nG = K // gsz
+    ctx = L.rocket_i4_ctx_create(1)
+    Wt = torch.randint(-8, 8, (N, K), dtype=torch.int8, device="cuda")
+    w = L.rocket_i4_weights_pack_gw(ctx, M, K, N, Wt.data_ptr(), gsz)
+    Aq = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+    asc = (torch.rand((M, 1), device="cuda") * 0.04 + 0.01).expand(M, nG).contiguous()
+    bsc = torch.rand((N, nG), device="cuda") * 0.015 + 0.005
+    Cf = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    fd3 = L.rocket_b200_ctx_fd(ctx, 0)
+    s3 = torch.cuda.ExternalStream(L.rocket_b200_stream(fd3))
+    run3 = lambda: L.rocket_matmul_int4_prepacked_gw(ctx, M, K, N, Aq.data_ptr(), asc.data_ptr(),
+                                                     bsc.data_ptr(), Cf.data_ptr(), w)
+    for _ in range(3):
+        run3()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    L.rocket_b200_profile_reset()
+    L.rocket_b200_profile_enable(1)
+    a.record(s3)
+    for _ in range(20):
+        run3()
+    b.record(s3)
+    torch.cuda.synchronize()
+    L.rocket_b200_profile_enable(0)
+    ms3 = a.elapsed_time(b) / 20
+    prof = rkb.profile_snapshot()
+    nk, kms = prof.get("wgemm_w4_f16_tcgen05", (1, 0.0))
+    out["config3_w4a8_gw"] = {"tops_call": 2 * M * N * K / ms3 / 1e9, "ms_call": ms3,
+                              "kernel_tops": 2 * M * N * K / (kms / max(nk, 1)) / 1e9,
+                              "kernel_frac_of_measured_f16": 2 * M * N * K / (kms / max(nk, 1)) / 1e9 / peaks["bf16_tflops"],
+                              "per_call_kernels": {k: v for k, v in prof.items() if v[0]},
+                              "note": "fp16 MMA after in-register int4 dequant: peak is the fp16 dense rate"}
+    L.rocket_i4_weights_free(ctx, w)
+    L.rocket_i4_ctx_free(ctx)
+
+    # config 1: int8 64x512x256 one-shot (latency)
+    import numpy as np
+    A = np.random.default_rng(0).integers(-128, 128, (64, 512), dtype=np.int8)
+    B = np.random.default_rng(1).integers(-128, 128, (256, 512), dtype=np.int8)
+    C = np.zeros((64, 256), np.int32)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    dC = torch.empty((64, 256), dtype=torch.int32, device="cuda")
+    t0 = time.perf_counter()
+    for _ in range(200):
+        dev.matmul_int8(64, 512, 256, dA, dB, dC)
+    dev_us = (time.perf_counter() - t0) / 200 * 1e6
+    t0 = time.perf_counter()
+    for _ in range(200):
+        dev.matmul_int8(64, 512, 256, A, B, C)
+    host_us = (time.perf_counter() - t0) / 200 * 1e6
+    exact = bool((C == (A.astype(np.int64) @ B.astype(np.int64).T).astype(np.int32)).all())
+    out["config1_int8_latency"] = {"us_per_call_device_ptrs": dev_us, "us_per_call_host_ptrs": host_us,
+                                   "bit_exact": exact,
+                                   "note": "16.8 MOP: latency-bound, TOPS not meaningful"}
+    dev.close()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return main_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,234 @@
+/*
+ * oracle.c -- CPU restatement of the reference's host computations for the
+ * matmul hot path of librocketnpu (gregordinary/rocket-userspace).
+ *
+ * TEST INFRASTRUCTURE ONLY.  tests/, __graft_entry__.smoke() and bench.py's
+ * CPU-baseline leg load this as the checker and the timed CPU baseline; the
+ * library (rocket-userspace_b200/) never links or calls it.
+ *
+ * Pinned against the reference's own gates: oracle/Makefile target `pin`
+ * compiles the reference's test programs unchanged against ref_stub.c, whose
+ * matmul entry points return this oracle's results; each gate then checks
+ * them with its own host loop, its own seeded inputs and its own tolerance
+ * (tests/golden/make_golden.py runs them and writes the fixtures).
+ */
+#define _GNU_SOURCE
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "oracle.h"
+
+/* ---- fp16 conversion (IEEE binary16, round to nearest even via _Float16) -- */
+float orc_h2f(uint16_t h)
+{
+    _Float16 f;
+    memcpy(&f, &h, 2);
+    return (float)f;
+}
+
+uint16_t orc_f2h(float x)
+{
+    _Float16 f = (_Float16)x;
+    uint16_t h;
+    memcpy(&h, &f, 2);
+    return h;
+}
+
+/* ---- generators ------------------------------------------------------------ */
+/* splitmix64 as in tests/matmul_correctness_matrix_rocket.c:50-56 */
+uint64_t orc_splitmix64(uint64_t *s)
+{
+    uint64_t z = (*s += 0x9E3779B97F4A7C15ULL);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    return z ^ (z >> 31);
+}
+
+/* glibc rand() stream, e.g. rand()%256-128 (tests/matmul_int8_tiled_rocket.c:36,60) */
+void orc_glibc_i8(unsigned seed, int lo, int span, size_t n, int8_t *out)
+{
+    srand(seed);
+    for (size_t i = 0; i < n; i++) out[i] = (int8_t)(rand() % span + lo);
+}
+
+void orc_uniform_i8(uint64_t seed, int lo, int hi, size_t n, int8_t *out)
+{
+    uint64_t s = seed;
+    const uint64_t span = (uint64_t)(hi - lo + 1);
+    for (size_t i = 0; i < n; i++) out[i] = (int8_t)(lo + (int)(orc_splitmix64(&s) % span));
+}
+
+static double u01(uint64_t *s) { return (double)(orc_splitmix64(s) >> 11) * (1.0 / 9007199254740992.0); }
+
+void orc_uniform_f32(uint64_t seed, float lo, float hi, size_t n, float *out)
+{
+    uint64_t s = seed;
+    for (size_t i = 0; i < n; i++) out[i] = (float)(lo + (hi - lo) * u01(&s));
+}
+
+/* Box-Muller normals */
+static double normal(uint64_t *s, int *have, double *spare)
+{
+    if (*have) { *have = 0; return *spare; }
+    double u1 = u01(s), u2 = u01(s);
+    if (u1 < 1e-300) u1 = 1e-300;
+    double r = sqrt(-2.0 * log(u1)), th = 2.0 * M_PI * u2;
+    *spare = r * sin(th);
+    *have = 1;
+    return r * cos(th);
+}
+
+void orc_normal_f16(uint64_t seed, float scale, size_t n, uint16_t *out)
+{
+    uint64_t s = seed;
+    int have = 0;
+    double spare = 0;
+    for (size_t i = 0; i < n; i++) out[i] = orc_f2h((float)(normal(&s, &have, &spare) * scale));
+}
+
+void orc_normal_f32(uint64_t seed, float mean, float std, size_t n, float *out)
+{
+    uint64_t s = seed;
+    int have = 0;
+    double spare = 0;
+    for (size_t i = 0; i < n; i++) out[i] = (float)(mean + std * normal(&s, &have, &spare));
+}
+
+/* ---- row-range threading --------------------------------------------------- */
+typedef struct {
+    void (*fn)(void *, int, int);
+    void *arg;
+    int r0, r1;
+} rows_job;
+
+static void *rows_thread(void *p)
+{
+    rows_job *j = p;
+    j->fn(j->arg, j->r0, j->r1);
+    return NULL;
+}
+
+static void run_rows(void (*fn)(void *, int, int), void *arg, int row0, int row1, int nthreads)
+{
+    if (nthreads <= 1 || row1 - row0 < 2) { fn(arg, row0, row1); return; }
+    if (nthreads > 256) nthreads = 256;
+    pthread_t th[256];
+    rows_job jb[256];
+    int rows = row1 - row0, per = (rows + nthreads - 1) / nthreads, nt = 0;
+    for (int t = 0; t < nthreads; t++) {
+        int a = row0 + t * per, b = a + per < row1 ? a + per : row1;
+        if (a >= b) break;
+        jb[t] = (rows_job){fn, arg, a, b};
+        if (pthread_create(&th[t], NULL, rows_thread, &jb[t]) != 0) { fn(arg, a, b); jb[t].fn = NULL; }
+        nt = t + 1;
+    }
+    for (int t = 0; t < nt; t++)
+        if (jb[t].fn) pthread_join(th[t], NULL);
+}
+
+/* ---- int8 x int8 -> int32 via int64 accumulation ----------------------------
+ * tests/matmul_int8_tiled_rocket.c:77-83 and tests/matmul_int8_rocket.c:60-69:
+ *   s = sum_k (int32)A[m,k] * (int32)B[n,k]  (int64), C = (int32)s            */
+typedef struct { int M, K, N; const int8_t *A, *B; int32_t *C; } i8_args;
+
+static void i8_rows(void *p, int r0, int r1)
+{
+    const i8_args *a = p;
+    for (int m = r0; m < r1; m++)
+        for (int n = 0; n < a->N; n++) {
+            const int8_t *x = a->A + (size_t)m * a->K, *y = a->B + (size_t)n * a->K;
+            int64_t s = 0;
+            for (int k = 0; k < a->K; k++) s += (int32_t)x[k] * (int32_t)y[k];
+            a->C[(size_t)m * a->N + n] = (int32_t)s;
+        }
+}
+
+void orc_matmul_int8(int M, int K, int N, const int8_t *A, const int8_t *B, int32_t *C, int row0,
+                     int row1, int nthreads)
+{
+    i8_args a = {M, K, N, A, B, C};
+    run_rows(i8_rows, &a, row0, row1 < 0 ? M : row1, nthreads);
+}
+
+/* ---- fp16 x fp16, fp32 accumulation in ascending k, fp16 store --------------
+ * tests/matmul_tiled_rocket.c:76-82 (R = fp32 sum) and :92 ((_Float16)R)     */
+typedef struct { int M, K, N; const uint16_t *A, *B; float *R; uint16_t *C16; } f16_args;
+
+static void f16_rows(void *p, int r0, int r1)
+{
+    const f16_args *a = p;
+    float *rowA = malloc((size_t)a->K * sizeof(float));
+    for (int m = r0; m < r1; m++) {
+        for (int k = 0; k < a->K; k++) rowA[k] = orc_h2f(a->A[(size_t)m * a->K + k]);
+        for (int n = 0; n < a->N; n++) {
+            const uint16_t *y = a->B + (size_t)n * a->K;
+            float s = 0.f;
+            for (int k = 0; k < a->K; k++) s += rowA[k] * orc_h2f(y[k]);
+            if (a->R) a->R[(size_t)m * a->N + n] = s;
+            if (a->C16) a->C16[(size_t)m * a->N + n] = orc_f2h(s);
+        }
+    }
+    free(rowA);
+}
+
+void orc_matmul_fp16(int M, int K, int N, const uint16_t *A, const uint16_t *B, float *R,
+                     uint16_t *C16, int row0, int row1, int nthreads)
+{
+    f16_args a = {M, K, N, A, B, R, C16};
+    run_rows(f16_rows, &a, row0, row1 < 0 ? M : row1, nthreads);
+}
+
+/* ---- group-wise: fp64 reference -------------------------------------------------
+ * tests/matmul_int8_groupwise_rocket.c:41-56 (ref_gw), also
+ * tests/matmul_int4_prepacked_gw_rocket.c:33-47:
+ *   ref[m,n] = sum_g (double)as[m,g] * (double)bs[n,g] * (double)ip_g,
+ *   ip_g = sum_{k in g} (long)A * (long)B                                         */
+typedef struct { int M, K, N, group; const int8_t *A, *B; const float *as, *bs; double *ref; } gw_args;
+
+static void gw_rows(void *p, int r0, int r1)
+{
+    const gw_args *a = p;
+    const int nG = a->K / a->group;
+    for (int m = r0; m < r1; m++)
+        for (int n = 0; n < a->N; n++) {
+            double acc = 0.0;
+            for (int g = 0; g < nG; g++) {
+                long ip = 0;
+                const int8_t *x = a->A + (size_t)m * a->K + (size_t)g * a->group;
+                const int8_t *y = a->B + (size_t)n * a->K + (size_t)g * a->group;
+                for (int k = 0; k < a->group; k++) ip += (long)x[k] * (long)y[k];
+                acc += (double)a->as[(size_t)m * nG + g] * (double)a->bs[(size_t)n * nG + g] * (double)ip;
+            }
+            a->ref[(size_t)m * a->N + n] = acc;
+        }
+}
+
+void orc_gw_ref(int M, int K, int N, int group, const int8_t *A, const int8_t *B, const float *as,
+                const float *bs, double *ref, int row0, int row1, int nthreads)
+{
+    gw_args a = {M, K, N, group, A, B, as, bs, ref};
+    run_rows(gw_rows, &a, row0, row1 < 0 ? M : row1, nthreads);
+}
+
+/* ---- group-wise: the reference library's own fp32 host accumulation ------------
+ * src/rocket_matmul.c:2846-2856 / src/rocket_prepacked_int8.c:620-632: for each
+ * K-group g in ascending order, Cf += as[m,g] * bs[n,g] * (float)partial_g, in
+ * fp32 and in that evaluation order ((as*bs)*partial).  With the K-tile equal
+ * to the group this is the value the NPU path returns.                        */
+void orc_gw_f32(int M, int K, int N, int group, const int8_t *A, const int8_t *B, const float *as,
+                const float *bs, float *Cf)
+{
+    const int nG = K / group;
+    for (size_t i = 0; i < (size_t)M * N; i++) Cf[i] = 0.f;
+    for (int g = 0; g < nG; g++)
+        for (int m = 0; m < M; m++)
+            for (int n = 0; n < N; n++) {
+                int32_t p = 0;
+                const int8_t *x = A + (size_t)m * K + (size_t)g * group;
+                const int8_t *y = B + (size_t)n * K + (size_t)g * group;
+                for (int k = 0; k < group; k++) p += (int32_t)x[k] * (int32_t)y[k];
+                Cf[(size_t)m * N + n] += as[(size_t)m * nG + g] * bs[(size_t)n * nG + g] * (float)p;
+            }
+}

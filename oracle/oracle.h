@@ -1,0 +1,42 @@
+/*
+ * oracle.h -- CPU restatement of the reference's host computations for the
+ * matmul hot path and the encoder ops.  TEST INFRASTRUCTURE ONLY: used by
+ * tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg as the
+ * checker / CPU baseline, never by the library.
+ */
+#ifndef RKB_ORACLE_H
+#define RKB_ORACLE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- generators ---- */
+uint64_t orc_splitmix64(uint64_t *state);
+/* glibc rand() streams as the reference gates draw them (srand(seed) first). */
+void orc_glibc_i8(unsigned seed, int lo, int span, size_t n, int8_t *out);  /* rand()%span + lo */
+void orc_uniform_i8(uint64_t seed, int lo, int hi, size_t n, int8_t *out);  /* [lo,hi] */
+void orc_uniform_f32(uint64_t seed, float lo, float hi, size_t n, float *out);
+void orc_normal_f16(uint64_t seed, float scale, size_t n, uint16_t *out);   /* N(0,1)*scale */
+void orc_normal_f32(uint64_t seed, float mean, float std, size_t n, float *out);
+
+/* ---- matmul restatements (C = A * B^T, row-major) ---- */
+void orc_matmul_int8(int M, int K, int N, const int8_t *A, const int8_t *B, int32_t *C,
+                     int row0, int row1, int nthreads);
+void orc_matmul_fp16(int M, int K, int N, const uint16_t *A, const uint16_t *B, float *R,
+                     uint16_t *C16, int row0, int row1, int nthreads);
+void orc_gw_ref(int M, int K, int N, int group, const int8_t *A, const int8_t *B,
+                const float *as, const float *bs, double *ref, int row0, int row1, int nthreads);
+void orc_gw_f32(int M, int K, int N, int group, const int8_t *A, const int8_t *B,
+                const float *as, const float *bs, float *Cf);
+
+/* fp16 helpers */
+float    orc_h2f(uint16_t h);
+uint16_t orc_f2h(float f);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

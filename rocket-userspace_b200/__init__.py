@@ -96,7 +96,17 @@ _SIGS = [
     ("rocket_matmul_int4_prepacked_gw", c_int, [_P, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
 ]
 
-EXTRA_SIGS: list = []   # second-tier ops register here (see ops.py)
+# rocket_b200.h extensions (no reference counterpart)
+_SIGS += [
+    ("rocket_b200_stream", c_void_p, [c_int]),
+    ("rocket_b200_device", c_int, [c_int]),
+    ("rocket_b200_ctx_fd", c_int, [c_void_p, c_int]),
+    ("rocket_b200_profile_enable", None, [c_int]),
+    ("rocket_b200_profile_reset", None, []),
+    ("rocket_b200_profile_get", c_int, [c_int, POINTER(c_char_p), POINTER(c_uint64), POINTER(ctypes.c_double)]),
+]
+
+EXTRA_SIGS: list = []
 
 
 def _load():
@@ -171,6 +181,17 @@ class Device:
     def matmul_int4_groupwise(self, M, K, N, A, B, a_scale, b_scale, Cf, group):
         return lib.rocket_matmul_int4_groupwise(self.fd, M, K, N, ptr(A), ptr(B), ptr(a_scale),
                                                 ptr(b_scale), ptr(Cf), group)
+
+
+def profile_snapshot() -> dict:
+    """{family: (launches, total_ms)} from the library's kernel profiler."""
+    out = {}
+    i = 0
+    name, n, ms = c_char_p(), c_uint64(), ctypes.c_double()
+    while lib.rocket_b200_profile_get(i, ctypes.byref(name), ctypes.byref(n), ctypes.byref(ms)) == 0:
+        out[name.value.decode()] = (n.value, ms.value)
+        i += 1
+    return out
 
 
 def plan(kind: str, M, K, N, group=None):

@@ -24,6 +24,13 @@ enum rkb_scratch_slot {
     RKB_SCR_ROW, RKB_SCR_WQ, RKB_SCR_WS, RKB_NSCR
 };
 
+/* Kernel families timed by the profiler (rocket_b200_profile_*). */
+enum rkb_kfam {
+    RKB_K_GEMM_I8 = 0, RKB_K_GEMM_F16, RKB_K_WGEMM_W4_F16, RKB_K_WGEMM_W8_F16, RKB_K_WGEMM_W4_I8,
+    RKB_K_PACK, RKB_K_PRESCALE, RKB_K_NORM, RKB_K_SOFTMAX, RKB_K_ATTN, RKB_K_ELEMWISE, RKB_NKFAM
+};
+#define RKB_PROF_SLOTS 64
+
 typedef struct rkb_handle {
     int in_use;
     int device;
@@ -33,6 +40,10 @@ typedef struct rkb_handle {
     void *scr[RKB_NSCR];
     size_t scr_cap[RKB_NSCR];
     struct { void *dptr; void *hptr; size_t size; int live; } bo[RKB_MAX_BOS];
+    /* profiler: event pairs recorded around launches, drained in rkb_finish */
+    cudaEvent_t ev[RKB_PROF_SLOTS][2];
+    int ev_fam[RKB_PROF_SLOTS];
+    int ev_used, ev_made;
 } rkb_handle;
 
 /* Handle table. */
@@ -59,6 +70,11 @@ int   rkb_stage_out_finish(rkb_handle *h, void *user, const void *dev, size_t by
  * then check the CUDA error state and the kernel error word.  Returns 0 or
  * ROCKET_E_DEVICE (with a log line naming `who`). */
 int rkb_finish(rkb_handle *h, const char *who);
+
+/* Profiler brackets: begin returns a slot (or -1 when profiling is off);
+ * end records the closing event for kernel family `fam`. */
+int  rkb_prof_begin(rkb_handle *h);
+void rkb_prof_end(rkb_handle *h, int slot, int fam);
 
 /* Count one device-reaching call and the kernels it launched. */
 void rkb_count(uint64_t calls, uint64_t kernels);

@@ -16,6 +16,7 @@
 #include <time.h>
 #include <unistd.h>
 
+#include "rocket_b200.h"
 #include "rkb_internal.h"
 
 static rkb_handle g_h[RKB_MAX_HANDLES];
@@ -23,6 +24,95 @@ static pthread_mutex_t g_lock = PTHREAD_MUTEX_INITIALIZER;
 static uint64_t g_calls, g_kernels;
 static __thread int g_aff_base;
 static long g_busy_poll_us = -1;
+
+/* ---- profiler ------------------------------------------------------------ */
+static int g_prof = -1;
+static pthread_mutex_t g_prof_lock = PTHREAD_MUTEX_INITIALIZER;
+static uint64_t g_prof_n[RKB_NKFAM];
+static double g_prof_ms[RKB_NKFAM];
+static const char *g_prof_name[RKB_NKFAM] = {
+    "gemm_i8_tcgen05", "gemm_f16_tcgen05", "wgemm_w4_f16_tcgen05", "wgemm_w8_f16_tcgen05",
+    "wgemm_w4_i8_tcgen05", "weight_pack", "act_prescale", "norm", "softmax", "attention",
+    "elementwise"};
+
+static int prof_on(void)
+{
+    if (g_prof < 0) g_prof = rkb_env_long("ROCKET_MM_PROFILE", 0) ? 1 : 0;
+    return g_prof;
+}
+
+void rocket_b200_profile_enable(int on) { g_prof = on ? 1 : 0; }
+
+void rocket_b200_profile_reset(void)
+{
+    pthread_mutex_lock(&g_prof_lock);
+    memset(g_prof_n, 0, sizeof g_prof_n);
+    memset(g_prof_ms, 0, sizeof g_prof_ms);
+    pthread_mutex_unlock(&g_prof_lock);
+}
+
+int rocket_b200_profile_get(int idx, const char **name, uint64_t *launches, double *total_ms)
+{
+    if (idx < 0 || idx >= RKB_NKFAM) return ROCKET_E_SHAPE;
+    pthread_mutex_lock(&g_prof_lock);
+    if (name) *name = g_prof_name[idx];
+    if (launches) *launches = g_prof_n[idx];
+    if (total_ms) *total_ms = g_prof_ms[idx];
+    pthread_mutex_unlock(&g_prof_lock);
+    return 0;
+}
+
+int rkb_prof_begin(rkb_handle *h)
+{
+    if (!prof_on() || h->ev_used >= RKB_PROF_SLOTS) return -1;
+    int s = h->ev_used;
+    if (s >= h->ev_made) {
+        if (cudaEventCreate(&h->ev[s][0]) != cudaSuccess || cudaEventCreate(&h->ev[s][1]) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+        h->ev_made = s + 1;
+    }
+    cudaEventRecord(h->ev[s][0], h->stream);
+    h->ev_used = s + 1;
+    return s;
+}
+
+void rkb_prof_end(rkb_handle *h, int slot, int fam)
+{
+    if (slot < 0) return;
+    cudaEventRecord(h->ev[slot][1], h->stream);
+    h->ev_fam[slot] = fam;
+}
+
+static void prof_drain(rkb_handle *h)
+{
+    if (!h->ev_used) return;
+    pthread_mutex_lock(&g_prof_lock);
+    for (int s = 0; s < h->ev_used; s++) {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, h->ev[s][0], h->ev[s][1]) == cudaSuccess) {
+            g_prof_n[h->ev_fam[s]] += 1;
+            g_prof_ms[h->ev_fam[s]] += ms;
+        } else {
+            cudaGetLastError();
+        }
+    }
+    pthread_mutex_unlock(&g_prof_lock);
+    h->ev_used = 0;
+}
+
+void *rocket_b200_stream(int fd)
+{
+    rkb_handle *h = rkb_get(fd);
+    return h ? (void *)h->stream : NULL;
+}
+
+int rocket_b200_device(int fd)
+{
+    rkb_handle *h = rkb_get(fd);
+    return h ? h->device : ROCKET_E_DEVICE;
+}
 
 long rkb_env_long(const char *name, long dflt)
 {
@@ -101,6 +191,10 @@ void rocket_close(int fd)
     for (int i = 0; i < RKB_NSCR; i++) cudaFree(h->scr[i]);
     for (int i = 0; i < RKB_MAX_BOS; i++)
         if (h->bo[i].live) { cudaFree(h->bo[i].dptr); cudaFreeHost(h->bo[i].hptr); }
+    for (int i = 0; i < h->ev_made; i++) {
+        cudaEventDestroy(h->ev[i][0]);
+        cudaEventDestroy(h->ev[i][1]);
+    }
     cudaStreamDestroy(h->stream);
     cudaFreeHost(h->err_host);
     pthread_mutex_lock(&g_lock);
@@ -209,6 +303,7 @@ int rkb_finish(rkb_handle *h, const char *who)
         ROCKET_LOGE("%s: CUDA error: %s\n", who, cudaGetErrorString(e != cudaSuccess ? e : cudaStreamQuery(h->stream)));
         return ROCKET_E_DEVICE;
     }
+    prof_drain(h);
     int ew = *(volatile int *)h->err_host;
     if (ew) {
         ROCKET_LOGE("%s: kernel pipeline wait expired (code %d)\n", who, ew);

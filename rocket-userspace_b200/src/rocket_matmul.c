@@ -65,7 +65,10 @@ int rkb_dense_on(rkb_handle *h, int in_kind, int out_kind, int M, int N, int K,
     d.M = M; d.N = N; d.K = K;
     d.A = dA; d.lda = lda; d.B = dB; d.ldb = ldb; d.C = dC; d.ldc = ldc;
     rkb_count(0, 1);
-    return rkb_gemm_run(&d, h->err_dev, h->stream);
+    int ps = rkb_prof_begin(h);
+    int rc = rkb_gemm_run(&d, h->err_dev, h->stream);
+    rkb_prof_end(h, ps, in_kind == RKB_IN_F16 ? RKB_K_GEMM_F16 : RKB_K_GEMM_I8);
+    return rc;
 }
 
 int rkb_rows_const(const float *a_scale, int M, int nG)
@@ -88,8 +91,11 @@ int rkb_gw_on(rkb_handle *h, int M, int N, int K, int group, int w_bits,
     void *ws = rkb_scratch(h, RKB_SCR_WS, rkb_wpack_scales_bytes(N, K));
     void *af = rkb_scratch(h, RKB_SCR_AUX, (size_t)M * K * 2);
     if (!dbs || !das || !ws || !af) return ROCKET_E_NOMEM;
+    int ps = rkb_prof_begin(h);
     int rc = rkb_wpack_scales(dbs, N, K, group, ws, h->stream);
+    rkb_prof_end(h, ps, RKB_K_PACK);
     float *row = NULL;
+    ps = rkb_prof_begin(h);
     if (!rc && a_rows_const) {
         row = rkb_scratch(h, RKB_SCR_ROW, (size_t)M * sizeof(float));
         if (!row) return ROCKET_E_NOMEM;
@@ -98,6 +104,7 @@ int rkb_gw_on(rkb_handle *h, int M, int N, int K, int group, int w_bits,
     } else if (!rc) {
         rc = rkb_prescale_a(dA, das, M, K, group, af, h->stream);
     }
+    rkb_prof_end(h, ps, RKB_K_PRESCALE);
     if (rc) return rc;
     rkb_wgemm_desc d;
     memset(&d, 0, sizeof d);
@@ -108,7 +115,10 @@ int rkb_gw_on(rkb_handle *h, int M, int N, int K, int group, int w_bits,
     d.C = dC; d.ldc = ldc; d.out_kind = out_kind;
     d.row_scale = row;
     rkb_count(0, a_rows_const ? 4 : 3);
-    return rkb_wgemm_run(&d, h->err_dev, h->stream);
+    ps = rkb_prof_begin(h);
+    rc = rkb_wgemm_run(&d, h->err_dev, h->stream);
+    rkb_prof_end(h, ps, w_bits == 4 ? RKB_K_WGEMM_W4_F16 : RKB_K_WGEMM_W8_F16);
+    return rc;
 }
 
 /* ---- one-shot entries ---------------------------------------------------- */
@@ -189,7 +199,9 @@ static int oneshot_gw(const char *who, int fd, int w_bits, int M, int K, int N, 
     void *dC = rkb_stage_out(h, RKB_SCR_C, Cf, (size_t)M * N * sizeof(float), &cb);
     if (!dA || !dB || !wq || !dC) return ROCKET_E_NOMEM;
     int rows_const = rkb_ptr_device(a_scale) < 0 ? rkb_rows_const(a_scale, M, nG) : 0;
+    int ps = rkb_prof_begin(h);
     int rc = rkb_wpack_codes(dB, N, K, w_bits, wq, h->stream);
+    rkb_prof_end(h, ps, RKB_K_PACK);
     if (!rc) rc = rkb_gw_on(h, M, N, K, group, w_bits, dA, a_scale, rows_const, wq, b_scale, dC, N,
                             RKB_OUT_F32);
     if (!rc) rc = rkb_stage_out_finish(h, Cf, dC, (size_t)M * N * sizeof(float), cb);

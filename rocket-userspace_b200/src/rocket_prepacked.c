@@ -25,6 +25,7 @@
 #include <string.h>
 
 #include "rocket_matmul.h"
+#include "rocket_b200.h"
 #include "rkb_internal.h"
 
 typedef enum { RW_F16, RW_I8, RW_I8_GW, RW_I4, RW_I4_GW } rw_kind;
@@ -86,6 +87,13 @@ static int rctx_init(rkb_rctx *c, int nthreads, int atom, const char *who)
     return 0;
 }
 
+int rocket_b200_ctx_fd(const void *ctx, int worker)
+{
+    const rkb_rctx *c = ctx;
+    if (!c || worker < 0 || worker >= c->nthreads) return ROCKET_E_SHAPE;
+    return c->fd[worker];
+}
+
 static void rctx_free(rkb_rctx *c)
 {
     for (int t = 0; t < c->nthreads; t++) rocket_close(c->fd[t]);
@@ -129,7 +137,9 @@ static int rweights_pack(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M
             w->bytes[t] = rkb_wpack_codes_bytes(nsub, K, bits);
             const void *dsrc = rkb_stage_in(h, RKB_SCR_B, src, raw);
             if (!dsrc || cudaMalloc(&w->dev[t], w->bytes[t]) != cudaSuccess) { rc = ROCKET_E_NOMEM; break; }
+            int ps = rkb_prof_begin(h);
             rc = rkb_wpack_codes(dsrc, nsub, K, bits, w->dev[t], h->stream);
+            rkb_prof_end(h, ps, RKB_K_PACK);
             if (rc) break;
         }
         rkb_count(1, 1);
@@ -210,7 +220,9 @@ static int rrun(const rkb_rctx *c, const rkb_rweights *w, int M, const rrun_args
             d.A = dA; d.lda = K; d.Wq = w->dev[t]; d.Ws = NULL;
             d.C = dC; d.ldc = ldc; d.out_kind = RKB_OUT_I32;
             rkb_count(0, 1);
+            int ps = rkb_prof_begin(h);
             rc = rkb_wgemm_run(&d, h->err_dev, h->stream);
+            rkb_prof_end(h, ps, RKB_K_WGEMM_W4_I8);
             break;
         }
         case RW_I8_GW:
