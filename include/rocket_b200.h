@@ -32,6 +32,29 @@ void  rocket_b200_profile_enable(int on);
 void  rocket_b200_profile_reset(void);
 int   rocket_b200_profile_get(int idx, const char **name, uint64_t *launches, double *total_ms);
 
+/* Group-wise int4 matmul that allocates nothing.  No counterpart in the
+ * reference.  For callers that may not call cudaMalloc (a runtime that owns all
+ * device memory through its own arena, a fixed memory budget, or a loop that
+ * must not allocate while it runs): the same computation as
+ * rocket_matmul_int4_groupwise, with its device scratch (packed codes, packed
+ * scales, pre-scaled activations) taken from one array compiled into the
+ * library -- 32 MiB on every GPU that loads it, held until the process exits.
+ *
+ *   - A, B, a_scale, b_scale and Cf must be device memory on the current CUDA
+ *     device (A and Cf 16-byte aligned); nothing is copied.
+ *   - A call needing more than the 32 MiB array (about N*K/2 + 2*M*K bytes)
+ *     returns ROCKET_E_NOMEM and does nothing.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); the call
+ *     waits for it before returning its status.
+ *   - The first call on a device looks up the array's device address; make
+ *     that first call before any stream capture.
+ *   - Every call on a device shares the one array, so calls that may overlap
+ *     on the GPU (other streams, other host threads) race: serialise them. */
+int rocket_b200_matmul_int4_groupwise_noalloc(int M, int K, int N, const int8_t *A,
+                                              const int8_t *B, const float *a_scale,
+                                              const float *b_scale, float *Cf, int group,
+                                              void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -104,6 +104,8 @@ _SIGS += [
     ("rocket_b200_profile_enable", None, [c_int]),
     ("rocket_b200_profile_reset", None, []),
     ("rocket_b200_profile_get", c_int, [c_int, POINTER(c_char_p), POINTER(c_uint64), POINTER(ctypes.c_double)]),
+    ("rocket_b200_matmul_int4_groupwise_noalloc", c_int,
+     [c_int, c_int, c_int, _P, _P, _P, _P, _P, c_int, _P]),
 ]
 
 EXTRA_SIGS: list = []
