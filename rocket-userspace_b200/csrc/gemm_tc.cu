@@ -22,6 +22,8 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <mutex>
+#include <cmath>
+#include <cstdlib>
 
 #include "rkb_ptx.cuh"
 #include "rkb_tmap.h"
@@ -286,17 +288,232 @@ int launch(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
     return 0;
 }
 
-// Tile-width choice: BN=256 unless that leaves most SMs idle for a shape
-// whose tile count would fill the GPU better with BN=128.
-inline int pick_bn(int M, int N) {
-    const int sms = 148;
-    const long t256 = static_cast<long>((M + BM - 1) / BM) * ((N + 255) / 256);
-    if (t256 >= sms) return 256;
-    const long t128 = static_cast<long>((M + BM - 1) / BM) * ((N + 127) / 128);
-    // waves-efficiency of each choice: tiles / (ceil(tiles/sms) * sms)
-    const double e256 = static_cast<double>(t256) / (((t256 + sms - 1) / sms) * sms);
-    const double e128 = static_cast<double>(t128) / (((t128 + sms - 1) / sms) * sms);
-    return (e128 > e256 * 1.15) ? 128 : 256;
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs (two SMs) computes a 256 x BN tile
+// with tcgen05.mma.cta_group::2 (M = 256).  CTA r loads rows r*128..+127 of the
+// A tile and rows r*BN/2..+BN/2-1 of the B tile into its own shared memory;
+// the leader's MMA reads both halves, and each CTA's TMEM receives its 128
+// output rows x BN columns.  Per SM this moves 16 + BN/2*128/1024 KB per
+// K-block instead of 16 + BN*128/1024 KB, which is what the single-CTA kernel
+// is limited by (L2 -> SM operand bandwidth).
+template <int BN>
+struct Cfg2 {
+    static constexpr int BNH = BN / 2;
+    static constexpr int A_BYTES = BM * BK_BYTES;
+    static constexpr int B_BYTES = BNH * BK_BYTES;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (BN == 256) ? 6 : 8;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+};
+
+template <int KIND, int OUT, int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+             const Args g) {
+    using C = Cfg2<BN>;
+    constexpr int STAGES = C::STAGES;
+    constexpr int BK_ELEMS = (KIND == RKB_IN_F16) ? 64 : 128;
+    constexpr uint32_t IDESC = (KIND == RKB_IN_F16) ? idesc_f16_f32acc(2 * BM, BN)
+                                                    : idesc_s8_s32acc(2 * BM, BN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
+    const uint32_t smem_base = smem_u32(smem);
+    auto sA = [&](int s) { return smem_base + s * C::STAGE_BYTES; };
+    auto sB = [&](int s) { return smem_base + s * C::STAGE_BYTES + C::A_BYTES; };
+    auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+    auto empty_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
+    auto tfull_bar = [&](int b) { return smem_u32(&bars[2 * STAGES + b]); };
+    auto tempty_bar = [&](int b) { return smem_u32(&bars[2 * STAGES + 2 + b]); };
+    const uint32_t drain_bar = smem_u32(&bars[2 * STAGES + 4]);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t peer = rank ^ 1u;
+    const bool leader = rank == 0;
+
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull_bar(b), 1);
+            mbar_init(tempty_bar(b), 8);   // 4 epilogue warps x 2 CTAs
+        }
+        mbar_init(drain_bar, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int num_tiles = g.m_tiles * g.n_tiles;
+    const int cluster_id = blockIdx.x >> 1;
+    const int nclusters = gridDim.x >> 1;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = cluster_id; t < num_tiles && ok; t += nclusters) {
+                const int mt = t % g.m_tiles, nt = t / g.m_tiles;
+                for (int kb = 0; kb < g.k_blocks; ++kb) {
+                    if (!mbar_wait(empty_bar(s), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) { ok = false; break; }
+                    const uint32_t lf = mapa_shared(full_bar(s), 0);
+                    if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * C::STAGE_BYTES);
+                    tma_load_2d_pair(sA(s), &tmA, kb * BK_ELEMS, mt * 2 * BM + rank * BM, lf);
+                    tma_load_2d_pair(sB(s), &tmB, kb * BK_ELEMS, nt * BN + rank * C::BNH, lf);
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            int it = 0;
+            for (int t = cluster_id; t < num_tiles && ok; t += nclusters, ++it) {
+                const int b = it & 1;
+                const uint32_t aph = (it >> 1) & 1;
+                if (!mbar_wait(tempty_bar(b), aph ^ 1, g.err, ERR_WAIT_MMA_ACC)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t dcol = tmem_base + b * BN;
+                for (int kb = 0; kb < g.k_blocks; ++kb) {
+                    if (!mbar_wait(full_bar(s), ph, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t adesc = smem_desc_sw128(sA(s));
+                    const uint64_t bdesc = smem_desc_sw128(sB(s));
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint64_t koff = static_cast<uint64_t>((k * 32) >> 4);
+                        const uint32_t acc = (kb | k) != 0;
+                        if (KIND == RKB_IN_F16) tc_mma_f16_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                        else                    tc_mma_i8_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                    }
+                    tc_commit_pair(empty_bar(s));
+                    tc_commit_pair(mapa_shared(empty_bar(s), peer));
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+                if (ok) {
+                    tc_commit_pair(tfull_bar(b));
+                    tc_commit_pair(mapa_shared(tfull_bar(b), peer));
+                }
+            }
+            if (!ok) {
+                tc_commit_pair(drain_bar);
+                mbar_wait_drain(drain_bar, 0);
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        int it = 0;
+        const uint32_t lempty0 = mapa_shared(tempty_bar(0), 0);
+        const uint32_t lempty1 = mapa_shared(tempty_bar(1), 0);
+        for (int t = cluster_id; t < num_tiles; t += nclusters, ++it) {
+            const int b = it & 1;
+            const uint32_t aph = (it >> 1) & 1;
+            if (!mbar_wait(tfull_bar(b), aph, g.err, ERR_WAIT_EPILOGUE)) break;
+            tc_fence_after();
+            const int mt = t % g.m_tiles, nt = t / g.m_tiles;
+            const int row = mt * 2 * BM + rank * BM + q * 32 + lane;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(tbase + c, r);
+                tmem_ld_wait();
+                const int col = nt * BN + c;
+                if (col < g.N) store_chunk<OUT>(g, row, col, r);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(b ? lempty1 : lempty0);
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    }
+}
+
+template <int KIND, int OUT, int BN>
+int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
+    using C = Cfg2<BN>;
+    static std::once_flag attr_once[16];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(attr_once[dev & 15], [] {
+        cudaFuncSetAttribute(gemm2_kernel<KIND, OUT, BN>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    });
+    const int esize = (KIND == RKB_IN_F16) ? 2 : 1;
+    const CUtensorMapDataType dt =
+        (KIND == RKB_IN_F16) ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    CUtensorMap ta, tb;
+    if (make_tmap_2d(&ta, d->A, dt, esize, d->K, d->M, d->lda, BK_BYTES / esize, BM) ||
+        make_tmap_2d(&tb, d->B, dt, esize, d->K, d->N, d->ldb, BK_BYTES / esize, C::BNH))
+        return ROCKET_E_SHAPE;
+    Args g;
+    g.M = d->M; g.N = d->N; g.K = d->K;
+    g.m_tiles = (d->M + 2 * BM - 1) / (2 * BM);
+    g.n_tiles = (d->N + BN - 1) / BN;
+    g.k_blocks = (d->K * esize + BK_BYTES - 1) / BK_BYTES;
+    g.C = d->C; g.ldc = d->ldc;
+    g.row_scale = d->row_scale; g.col_scale = d->col_scale;
+    g.err = err;
+    const int tiles = g.m_tiles * g.n_tiles;
+    const int pairs = rkb_device_sm_count(dev) / 2;
+    const int grid = 2 * (tiles < pairs ? tiles : pairs);
+    gemm2_kernel<KIND, OUT, BN><<<grid, NUM_THREADS, C::SMEM, stream>>>(ta, tb, g);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        fprintf(stderr, "rkb gemm2 launch: %s\n", cudaGetErrorString(e));
+        return ROCKET_E_DEVICE;
+    }
+    return 0;
+}
+
+// Kernel choice by estimated time: waves x work per tile / assumed efficiency
+// (single-CTA tiles 128 x BN, CTA-pair tiles 256 x BN on two SMs).  Returns
+// 0x100 | BN for the pair kernel, BN for the single-CTA one.
+inline int pick_variant(int M, int N) {
+    if (const char *e = getenv("ROCKET_GEMM_VARIANT")) {
+        int v = atoi(e);
+        if (v == 128 || v == 256 || v == 0x180 || v == 0x200 || v == 384 || v == 512) return v == 384 ? 0x180 : v == 512 ? 0x200 : v;
+    }
+    const double sms = 148.0;
+    struct Opt { int code, tm, bn, unit; double eff; } opts[] = {
+        {256, 128, 256, 1, 0.66}, {128, 128, 128, 1, 0.60},
+        {0x200, 256, 256, 2, 0.82}, {0x180, 256, 128, 2, 0.76}};
+    double best = 1e300;
+    int code = 256;
+    for (const Opt &o : opts) {
+        const double tiles = std::ceil(M / double(o.tm)) * std::ceil(N / double(o.bn));
+        const double units = sms / o.unit;
+        const double waves = std::ceil(tiles / units);
+        const double t = waves * (double(o.tm) * o.bn / o.unit) / o.eff;
+        if (t < best * 0.999) { best = t; code = o.code; }
+    }
+    return code;
 }
 
 }  // namespace dense
@@ -306,10 +523,14 @@ extern "C" int rkb_gemm_run(const rkb_gemm_desc *d, int *err, cudaStream_t strea
     using namespace rkb::dense;
     if (d->M <= 0 || d->N <= 0 || d->K <= 0) return ROCKET_E_SHAPE;
     if ((d->N & 7) || (d->ldc & 7)) return ROCKET_E_SHAPE;
-    const int bn = pick_bn(d->M, d->N);
-#define RKB_DISPATCH(KIND, OUT)                                            \
-    return bn == 256 ? launch<KIND, OUT, 256>(d, err, stream)              \
-                     : launch<KIND, OUT, 128>(d, err, stream)
+    const int v = pick_variant(d->M, d->N);
+#define RKB_DISPATCH(KIND, OUT)                                                   \
+    switch (v) {                                                                  \
+    case 0x200: return launch2<KIND, OUT, 256>(d, err, stream);                   \
+    case 0x180: return launch2<KIND, OUT, 128>(d, err, stream);                   \
+    case 128:   return launch<KIND, OUT, 128>(d, err, stream);                    \
+    default:    return launch<KIND, OUT, 256>(d, err, stream);                    \
+    }
     if (d->in_kind == RKB_IN_F16) {
         if (d->out_kind == RKB_OUT_F16) { RKB_DISPATCH(RKB_IN_F16, RKB_OUT_F16); }
         if (d->out_kind == RKB_OUT_F32) { RKB_DISPATCH(RKB_IN_F16, RKB_OUT_F32); }
