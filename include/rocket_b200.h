@@ -22,6 +22,19 @@ int   rocket_b200_device(int fd);
  * (all three share one layout), or ROCKET_E_SHAPE when out of range. */
 int   rocket_b200_ctx_fd(const void *ctx, int worker);
 
+/* Deferred completion for this host thread.  The reference API is synchronous
+ * and stays so by default.  With rocket_b200_set_async(1), a dense or
+ * per-channel resident matmul whose operands are ALL device memory on the
+ * worker GPUs (nothing to copy to or from the host) returns right after its
+ * kernels are enqueued on the handle's stream; its status -- including a
+ * bounded-wait expiry inside a kernel -- is returned by the next
+ * rocket_b200_sync(fd) / rocket_b200_ctx_sync(ctx).  Calls that stage host
+ * memory, and the group-wise entries, still wait before returning.  Work on
+ * one handle runs in call order, so back-to-back calls queue without gaps. */
+void  rocket_b200_set_async(int on);
+int   rocket_b200_sync(int fd);
+int   rocket_b200_ctx_sync(const void *ctx);
+
 /* Kernel profiling (the device-side analogue of the reference's
  * ROCKET_MM_PROFILE, src/rocket_matmul.c:74-125).  While enabled (also by the
  * environment variable ROCKET_MM_PROFILE=1), every kernel the library launches
@@ -54,6 +67,23 @@ int rocket_b200_matmul_int4_groupwise_noalloc(int M, int K, int N, const int8_t 
                                               const int8_t *B, const float *a_scale,
                                               const float *b_scale, float *Cf, int group,
                                               void *stream);
+
+/* Batched encoder block: nb independent sequences of T tokens stacked along
+ * rows (x and out are [nb*T, d]); every projection runs once over all nb*T
+ * rows and attention stays within each sequence.  Same arguments and result
+ * as nb calls of rocket_encoder_block_fp16 (include/rocket_encoder.h).  No
+ * counterpart in the reference, whose API has no batch dimension. */
+int rocket_b200_encoder_block_batched_fp16(int fd, int nb, int T, int d, int n_head, int d_ff,
+                                           const void *x,
+                                           const void *ln1_g, const void *ln1_b,
+                                           const void *Wq, const void *bq,
+                                           const void *Wk, const void *bk,
+                                           const void *Wv, const void *bv,
+                                           const void *Wo, const void *bo,
+                                           const void *ln2_g, const void *ln2_b,
+                                           const void *Wf1, const void *bf1,
+                                           const void *Wf2, const void *bf2,
+                                           float eps, void *out);
 
 #ifdef __cplusplus
 }

@@ -133,3 +133,118 @@ def max_abs_rel(got, ref):
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-300))
+
+
+# ---- encoder ops ----
+def _sig_enc():
+    P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    sigs = {
+        "orc_layernorm_f16": [I, I, P, P, P, F, P],
+        "orc_rmsnorm_f16": [I, I, P, P, F, P],
+        "orc_softmax_f16": [I, I, P, I, P],
+        "orc_activation_f16": [I, P, P, ctypes.c_size_t],
+        "orc_mha_self_f16": [I, I, I] + [P] * 10,
+        "orc_ffn_f16": [I, I, I, P, P, P, P, I, P],
+        "orc_encoder_block_f16": [I, I, I, I] + [P] * 17 + [F, P],
+    }
+    for n, a in sigs.items():
+        getattr(lib, n).restype = None
+        getattr(lib, n).argtypes = a
+
+
+_sig_enc()
+
+
+def _h(a):
+    return None if a is None else np.ascontiguousarray(a, np.float16).ctypes.data
+
+
+def layernorm(x, g, b, eps):
+    M, H = x.shape
+    y = np.empty_like(x, dtype=np.float16)
+    lib.orc_layernorm_f16(M, H, _h(x), _h(g), _h(b), eps, y.ctypes.data)
+    return y
+
+
+def rmsnorm(x, w, eps):
+    M, H = x.shape
+    y = np.empty_like(x, dtype=np.float16)
+    lib.orc_rmsnorm_f16(M, H, _h(x), _h(w), eps, y.ctypes.data)
+    return y
+
+
+def softmax(x, log_mode=False):
+    M, N = x.shape
+    y = np.empty_like(x, dtype=np.float16)
+    lib.orc_softmax_f16(M, N, _h(x), int(log_mode), y.ctypes.data)
+    return y
+
+
+def activation(kind, x):
+    y = np.empty_like(x, dtype=np.float16)
+    lib.orc_activation_f16(kind, _h(x), y.ctypes.data, x.size)
+    return y
+
+
+def mha_self(x, Wq, bq, Wk, bk, Wv, bv, Wo, bo, n_head):
+    T, d = x.shape
+    y = np.empty((T, d), np.float16)
+    lib.orc_mha_self_f16(T, d, n_head, _h(x), _h(Wq), _h(bq), _h(Wk), _h(bk), _h(Wv), _h(bv),
+                         _h(Wo), _h(bo), y.ctypes.data)
+    return y
+
+
+def ffn(x, Wg, Wu, Wd, kind):
+    M, H = x.shape
+    I = Wg.shape[0]
+    y = np.empty((M, H), np.float16)
+    lib.orc_ffn_f16(M, H, I, _h(x), _h(Wg), _h(Wu), _h(Wd), kind, y.ctypes.data)
+    return y
+
+
+def encoder_block(x, p, n_head, eps=1e-5):
+    """p: dict of ln1_g ln1_b Wq bq Wk bk Wv bv Wo bo ln2_g ln2_b W1 b1 W2 b2 (fp16 arrays)."""
+    T, d = x.shape
+    dff = p["W1"].shape[0]
+    y = np.empty((T, d), np.float16)
+    keys = ["ln1_g", "ln1_b", "Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo", "ln2_g", "ln2_b",
+            "W1", "b1", "W2", "b2"]
+    lib.orc_encoder_block_f16(T, d, n_head, dff, _h(x), *[_h(p.get(k)) for k in keys], eps, y.ctypes.data)
+    return y
+
+
+def encoder_params(T, d, nh, dff, seed):
+    """Seeded encoder-block inputs: x ~ N(0,1), weights and biases ~ N(0, 0.02),
+    LN gamma = 1, beta = 0 (the BASELINE config-4 distributions)."""
+    p = {"x": normal_f16(seed, 1.0, (T, d)),
+         "ln1_g": np.ones(d, np.float16), "ln1_b": np.zeros(d, np.float16),
+         "ln2_g": np.ones(d, np.float16), "ln2_b": np.zeros(d, np.float16)}
+    for i, (k, shp) in enumerate([("Wq", (d, d)), ("Wk", (d, d)), ("Wv", (d, d)), ("Wo", (d, d)),
+                                  ("W1", (dff, d)), ("W2", (d, dff))]):
+        p[k] = normal_f16(seed + 10 + i, 0.02, shp)
+    for i, (k, n) in enumerate([("bq", d), ("bk", d), ("bv", d), ("bo", d), ("b1", dff), ("b2", d)]):
+        p[k] = normal_f16(seed + 30 + i, 0.02, (n,))
+    return p
+
+
+def encoder_golden_inputs():
+    """The seeded inputs of tests/golden/encoder_golden.npz (outputs only are stored)."""
+    d = {}
+    d["ln_x"] = normal_f16(101, 2.0, (37, 512))
+    d["ln_g"] = normal_f16(102, 1.0, (512,))
+    d["ln_b"] = normal_f16(103, 0.5, (512,))
+    d["sm_x"] = normal_f16(104, 3.0, (21, 1500))
+    a = normal_f16(105, 3.0, (4096,))
+    d["act_x"] = a
+    d["act_xp"] = (np.abs(a.astype(np.float32)) + 0.1).astype(np.float16)
+    d["mha"] = encoder_params(40, 128, 2, 256, 200)
+    d["ffn_x"] = normal_f16(300, 1.0, (16, 128))
+    d["ffn_Wg"] = normal_f16(301, 0.05, (256, 128))
+    d["ffn_Wu"] = normal_f16(302, 0.05, (256, 128))
+    d["ffn_Wd"] = normal_f16(303, 0.05, (128, 256))
+    d["enc"] = encoder_params(64, 256, 4, 1024, 400)
+    return d
+
+
+ACT_KINDS = [0, 1, 2, 3, 4, 5, 7, 8, 9, 10, 11, 12, 13, 14, 15, 18]
+POSITIVE_KINDS = (7, 8, 9, 18)

@@ -232,3 +232,190 @@ void orc_gw_f32(int M, int K, int N, int group, const int8_t *A, const int8_t *B
                 Cf[(size_t)m * N + n] += as[(size_t)m * nG + g] * bs[(size_t)n * nG + g] * (float)p;
             }
 }
+
+/* =========================================================================
+ * Encoder ops: fp64 host definitions, fp16 in / fp16 out.  Each restates the
+ * reference's public host reference named beside it (pinned against those
+ * functions themselves by tests/test_oracle_encoder_pin.py).
+ * ========================================================================= */
+static double hd(uint16_t h) { return (double)orc_h2f(h); }
+static uint16_t dh16(double v)
+{
+    _Float16 f = (_Float16)v;   /* one rounding, double -> half, as the reference stores */
+    uint16_t h;
+    memcpy(&h, &f, 2);
+    return h;
+}
+
+/* src/rocket_norm.c:132-150 (rocket_layernorm_ref_fp16): E[x^2]-mean^2 variance, clamped at 0 */
+void orc_layernorm_f16(int M, int H, const uint16_t *x, const uint16_t *g, const uint16_t *b,
+                       float eps, uint16_t *y)
+{
+    for (int m = 0; m < M; m++) {
+        const uint16_t *r = x + (size_t)m * H;
+        double s1 = 0, s2 = 0;
+        for (int i = 0; i < H; i++) { double v = hd(r[i]); s1 += v; s2 += v * v; }
+        double mean = s1 / H, var = s2 / H - mean * mean;
+        if (var < 0) var = 0;
+        double inv = 1.0 / sqrt(var + (double)eps);
+        for (int i = 0; i < H; i++)
+            y[(size_t)m * H + i] = dh16((hd(r[i]) - mean) * inv * hd(g[i]) + (b ? hd(b[i]) : 0.0));
+    }
+}
+
+/* src/rocket_norm.c:57-70 (rocket_rmsnorm_ref_fp16) */
+void orc_rmsnorm_f16(int M, int H, const uint16_t *x, const uint16_t *w, float eps, uint16_t *y)
+{
+    for (int m = 0; m < M; m++) {
+        const uint16_t *r = x + (size_t)m * H;
+        double s2 = 0;
+        for (int i = 0; i < H; i++) s2 += hd(r[i]) * hd(r[i]);
+        double inv = 1.0 / sqrt(s2 / H + (double)eps);
+        for (int i = 0; i < H; i++) y[(size_t)m * H + i] = dh16(hd(r[i]) * inv * hd(w[i]));
+    }
+}
+
+/* src/rocket_softmax.c:23-35 and :80-92 (softmax / log-softmax, row max shift) */
+void orc_softmax_f16(int M, int N, const uint16_t *x, int log_mode, uint16_t *y)
+{
+    for (int m = 0; m < M; m++) {
+        const uint16_t *r = x + (size_t)m * N;
+        double mx = -INFINITY, s = 0;
+        for (int i = 0; i < N; i++) if (hd(r[i]) > mx) mx = hd(r[i]);
+        for (int i = 0; i < N; i++) s += exp(hd(r[i]) - mx);
+        for (int i = 0; i < N; i++)
+            y[(size_t)m * N + i] = dh16(log_mode ? hd(r[i]) - (mx + log(s)) : exp(hd(r[i]) - mx) / s);
+    }
+}
+
+/* src/rocket_activation.c:48-77 (act_eval) */
+double orc_act(int kind, double x)
+{
+    double hs = x / 6.0 + 0.5;
+    hs = hs < 0 ? 0 : (hs > 1 ? 1 : hs);
+    double sp = x > 0 ? x + log1p(exp(-x)) : log1p(exp(x));
+    switch (kind) {
+    case 0: return 1.0 / (1.0 + exp(-x));
+    case 1: return hs;
+    case 2: return x * hs;
+    case 3: return x * (1.0 / (1.0 + exp(-x)));
+    case 4: return tanh(x);
+    case 5: return 0.5 * x * (1.0 + erf(x / 1.4142135623730951));
+    case 7: return x > 0 ? sqrt(x) : 0;
+    case 8: return x > 0 ? 1.0 / sqrt(x) : 0;
+    case 9: return x != 0 ? 1.0 / x : 0;
+    case 10: return exp(x);
+    case 11: return 0.5 * (1.0 + erf(x / 1.4142135623730951));
+    case 12: return sp;
+    case 13: return tanh(sp);
+    case 14: return x * tanh(sp);
+    case 15: return fabs(x);
+    case 18: return x > 0 ? log(x) : 0;
+    default: return 0;
+    }
+}
+
+void orc_activation_f16(int kind, const uint16_t *x, uint16_t *y, size_t n)
+{
+    for (size_t i = 0; i < n; i++) y[i] = dh16(orc_act(kind, hd(x[i])));
+}
+
+/* the FFN / encoder MLP activation (src/rocket_ffn.c:23-27, src/rocket_encoder.c:22):
+ * GELU as 0.5 x (1 + erf(x / sqrt 2)) written with M_SQRT1_2, SiLU as x / (1 + e^-x) */
+static double act_mlp(int kind, double g)
+{
+    if (kind == 5) return 0.5 * g * (1.0 + erf(g * M_SQRT1_2));
+    return g / (1.0 + exp(-g));
+}
+
+/* y[T, N] = x[T, K] W[N, K]^T (+ b), fp64 */
+static void lin64(int T, int K, int N, const double *x, const uint16_t *W, const uint16_t *b, double *y)
+{
+    for (int t = 0; t < T; t++)
+        for (int n = 0; n < N; n++) {
+            double a = 0;
+            const uint16_t *w = W + (size_t)n * K;
+            for (int k = 0; k < K; k++) a += x[(size_t)t * K + k] * hd(w[k]);
+            y[(size_t)t * N + n] = a + (b ? hd(b[n]) : 0.0);
+        }
+}
+
+/* src/rocket_attn.c:41-84 (rocket_mha_self_ref_fp16): q/k/v projections, per-head
+ * softmax(q k^T / sqrt(dh)) v in fp64, output projection; one fp16 rounding */
+void orc_mha_self_f16(int T, int d, int nh, const uint16_t *x, const uint16_t *Wq, const uint16_t *bq,
+                      const uint16_t *Wk, const uint16_t *bk, const uint16_t *Wv, const uint16_t *bv,
+                      const uint16_t *Wo, const uint16_t *bo, uint16_t *out)
+{
+    const int dhd = d / nh;
+    const size_t Td = (size_t)T * d;
+    double *xd = malloc(Td * sizeof(double)), *q = malloc(Td * sizeof(double));
+    double *k = malloc(Td * sizeof(double)), *v = malloc(Td * sizeof(double));
+    double *ctx = malloc(Td * sizeof(double)), *p = malloc((size_t)T * sizeof(double));
+    double *o = malloc(Td * sizeof(double));
+    for (size_t i = 0; i < Td; i++) xd[i] = hd(x[i]);
+    lin64(T, d, d, xd, Wq, bq, q);
+    lin64(T, d, d, xd, Wk, bk, k);
+    lin64(T, d, d, xd, Wv, bv, v);
+    const double sc = 1.0 / sqrt((double)dhd);
+    for (int h = 0; h < nh; h++)
+        for (int i = 0; i < T; i++) {
+            double mx = -INFINITY, sum = 0;
+            for (int j = 0; j < T; j++) {
+                double s = 0;
+                for (int c = 0; c < dhd; c++) s += q[(size_t)i * d + h * dhd + c] * k[(size_t)j * d + h * dhd + c];
+                p[j] = s * sc;
+                if (p[j] > mx) mx = p[j];
+            }
+            for (int j = 0; j < T; j++) { p[j] = exp(p[j] - mx); sum += p[j]; }
+            for (int c = 0; c < dhd; c++) {
+                double a = 0;
+                for (int j = 0; j < T; j++) a += p[j] * v[(size_t)j * d + h * dhd + c];
+                ctx[(size_t)i * d + h * dhd + c] = a / sum;
+            }
+        }
+    lin64(T, d, d, ctx, Wo, bo, o);
+    for (size_t i = 0; i < Td; i++) out[i] = dh16(o[i]);
+    free(xd); free(q); free(k); free(v); free(ctx); free(p); free(o);
+}
+
+/* src/rocket_ffn.c:58-82 (rocket_ffn_ref_fp16): act(x Wg^T) * (x Wu^T), then Wd, fp64 */
+void orc_ffn_f16(int M, int H, int I, const uint16_t *x, const uint16_t *Wg, const uint16_t *Wu,
+                 const uint16_t *Wd, int kind, uint16_t *out)
+{
+    double *xd = malloc((size_t)M * H * sizeof(double)), *g = malloc((size_t)M * I * sizeof(double));
+    double *u = malloc((size_t)M * I * sizeof(double)), *o = malloc((size_t)M * H * sizeof(double));
+    for (size_t i = 0; i < (size_t)M * H; i++) xd[i] = hd(x[i]);
+    lin64(M, H, I, xd, Wg, NULL, g);
+    lin64(M, H, I, xd, Wu, NULL, u);
+    for (size_t i = 0; i < (size_t)M * I; i++) g[i] = act_mlp(kind, g[i]) * u[i];
+    lin64(M, I, H, g, Wd, NULL, o);
+    for (size_t i = 0; i < (size_t)M * H; i++) out[i] = dh16(o[i]);
+    free(xd); free(g); free(u); free(o);
+}
+
+/* src/rocket_encoder.c:79-108 (rocket_encoder_block_ref_fp16): pre-norm block;
+ * the attention half rounds to fp16 where the reference does (LN output, MHA
+ * output, residual sum), the MLP half stays fp64 until the final store */
+void orc_encoder_block_f16(int T, int d, int nh, int dff, const uint16_t *x,
+                           const uint16_t *g1, const uint16_t *b1, const uint16_t *Wq,
+                           const uint16_t *bq, const uint16_t *Wk, const uint16_t *bk,
+                           const uint16_t *Wv, const uint16_t *bv, const uint16_t *Wo,
+                           const uint16_t *bo, const uint16_t *g2, const uint16_t *b2,
+                           const uint16_t *W1, const uint16_t *c1, const uint16_t *W2,
+                           const uint16_t *c2, float eps, uint16_t *out)
+{
+    const size_t Td = (size_t)T * d;
+    uint16_t *ln = malloc(Td * 2), *attn = malloc(Td * 2), *xa = malloc(Td * 2);
+    double *lnd = malloc(Td * sizeof(double)), *f1 = malloc((size_t)T * dff * sizeof(double));
+    double *f2 = malloc(Td * sizeof(double));
+    orc_layernorm_f16(T, d, x, g1, b1, eps, ln);
+    orc_mha_self_f16(T, d, nh, ln, Wq, bq, Wk, bk, Wv, bv, Wo, bo, attn);
+    for (size_t i = 0; i < Td; i++) xa[i] = dh16(hd(x[i]) + hd(attn[i]));
+    orc_layernorm_f16(T, d, xa, g2, b2, eps, ln);
+    for (size_t i = 0; i < Td; i++) lnd[i] = hd(ln[i]);
+    lin64(T, d, dff, lnd, W1, c1, f1);
+    for (size_t i = 0; i < (size_t)T * dff; i++) f1[i] = act_mlp(5, f1[i]);
+    lin64(T, dff, d, f1, W2, NULL, f2);
+    for (size_t i = 0; i < Td; i++) out[i] = dh16(hd(xa[i]) + f2[i] + (c2 ? hd(c2[i % d]) : 0.0));
+    free(ln); free(attn); free(xa); free(lnd); free(f1); free(f2);
+}

@@ -36,6 +36,26 @@ void orc_gw_f32(int M, int K, int N, int group, const int8_t *A, const int8_t *B
 float    orc_h2f(uint16_t h);
 uint16_t orc_f2h(float f);
 
+/* ---- encoder ops (fp64 host definitions; fp16 in / out) ---- */
+void orc_layernorm_f16(int M, int H, const uint16_t *x, const uint16_t *g, const uint16_t *b,
+                       float eps, uint16_t *y);
+void orc_rmsnorm_f16(int M, int H, const uint16_t *x, const uint16_t *w, float eps, uint16_t *y);
+void orc_softmax_f16(int M, int N, const uint16_t *x, int log_mode, uint16_t *y);
+double orc_act(int kind, double x);
+void orc_activation_f16(int kind, const uint16_t *x, uint16_t *y, size_t n);
+void orc_mha_self_f16(int T, int d, int nh, const uint16_t *x, const uint16_t *Wq, const uint16_t *bq,
+                      const uint16_t *Wk, const uint16_t *bk, const uint16_t *Wv, const uint16_t *bv,
+                      const uint16_t *Wo, const uint16_t *bo, uint16_t *out);
+void orc_ffn_f16(int M, int H, int I, const uint16_t *x, const uint16_t *Wg, const uint16_t *Wu,
+                 const uint16_t *Wd, int kind, uint16_t *out);
+void orc_encoder_block_f16(int T, int d, int nh, int dff, const uint16_t *x,
+                           const uint16_t *g1, const uint16_t *b1, const uint16_t *Wq,
+                           const uint16_t *bq, const uint16_t *Wk, const uint16_t *bk,
+                           const uint16_t *Wv, const uint16_t *bv, const uint16_t *Wo,
+                           const uint16_t *bo, const uint16_t *g2, const uint16_t *b2,
+                           const uint16_t *W1, const uint16_t *c1, const uint16_t *W2,
+                           const uint16_t *c2, float eps, uint16_t *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -104,9 +104,37 @@ _SIGS += [
     ("rocket_b200_profile_enable", None, [c_int]),
     ("rocket_b200_profile_reset", None, []),
     ("rocket_b200_profile_get", c_int, [c_int, POINTER(c_char_p), POINTER(c_uint64), POINTER(ctypes.c_double)]),
+    ("rocket_b200_set_async", None, [c_int]),
+    ("rocket_b200_sync", c_int, [c_int]),
+    ("rocket_b200_ctx_sync", c_int, [c_void_p]),
     ("rocket_b200_matmul_int4_groupwise_noalloc", c_int,
      [c_int, c_int, c_int, _P, _P, _P, _P, _P, c_int, _P]),
 ]
+
+# encoder ops: rocket_norm.h, rocket_softmax.h, rocket_activation.h, rocket_ffn.h,
+# rocket_attn.h, rocket_encoder.h (+ the batched rocket_b200.h form)
+_F = ctypes.c_float
+_SIGS += [
+    ("rocket_layernorm_fp16", c_int, [c_int, c_int, c_int, _P, _P, _P, _F, _P]),
+    ("rocket_rmsnorm_fp16", c_int, [c_int, c_int, c_int, _P, _P, _F, _P]),
+    ("rocket_softmax_fp16", c_int, [c_int, c_int, c_int, _P, _P]),
+    ("rocket_logsoftmax_fp16", c_int, [c_int, c_int, c_int, _P, _P]),
+    ("rocket_activation_fp16", c_int, [c_int, c_int, _P, _P, c_int]),
+    ("rocket_ew_mul_fp16", c_int, [c_int, _P, _P, _P, c_int]),
+    ("rocket_ew_add_fp16", c_int, [c_int, _P, _P, _P, c_int]),
+    ("rocket_ew_sub_fp16", c_int, [c_int, _P, _P, _P, c_int]),
+    ("rocket_geglu_fp16", c_int, [c_int, _P, _P, c_int, _P, c_int]),
+    ("rocket_ffn_fp16", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, _P]),
+    ("rocket_ffn_fp16_fused", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, _P]),
+    ("rocket_mlp_fp16_fused", c_int, [c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, _P]),
+    ("rocket_mha_self_fp16", c_int, [c_int, c_int, c_int, c_int] + [_P] * 10),
+    ("rocket_encoder_block_fp16", c_int, [c_int, c_int, c_int, c_int, c_int] + [_P] * 17 + [_F, _P]),
+    ("rocket_b200_encoder_block_batched_fp16", c_int,
+     [c_int, c_int, c_int, c_int, c_int, c_int] + [_P] * 17 + [_F, _P]),
+]
+
+ENCODER_KEYS = ["ln1_g", "ln1_b", "Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo", "ln2_g", "ln2_b",
+                "W1", "b1", "W2", "b2"]
 
 EXTRA_SIGS: list = []
 

@@ -1,0 +1,308 @@
+// attn_tc.cu -- fused multi-head self-attention core on the sm_100a tensor
+// cores: O = softmax(Q K^T * scale) V per (batch, head), never writing the
+// T x T score matrix to HBM.
+//
+// Replaces the attention inner loop of the reference's rocket_mha_self_fp16
+// (src/rocket_attn.c:92-176: per head a scores matmul, key padding to %32 with
+// -30000 masking, a composed NPU softmax, and a P.V matmul), whose definition
+// is the fp64 host loop at src/rocket_attn.c:41-84.
+//
+// One CTA = 128 queries of one (batch, head); head_dim 64.  Roles:
+//   warp 0      TMA: Q once; K and V^T blocks of 128 keys into a 2-deep ring
+//   warp 1      MMA issuer: S_j = Q K_j^T (M=128, N=128, fp32 in TMEM cols
+//               0..127), O_j = P_j V_j (M=128, N=64, TMEM cols 128..191); S_{j+1}
+//               is issued as soon as S_j has been read, so it overlaps the
+//               softmax of block j
+//   warps 2..5  softmax: each thread owns one query row: reads its 128 scores
+//               from TMEM, online max / exp2 / row-sum in fp32, writes P_j as
+//               fp16 into a 128-byte-swizzled shared tile for the P V MMA, and
+//               folds O_{j-1} from TMEM into its 64 fp32 output registers
+// Keys past T (the last block) are masked to -inf.  Inputs come from
+// rkb_split_heads: Q, K [B*H, Tp, 64] and V^T [B*H, 64, Tp], zero-padded.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <mutex>
+
+#include "rkb_ptx.cuh"
+#include "rkb_tmap.h"
+#include "../src/rkb_kernels.h"
+#include "../../include/rocket_npu.h"
+
+namespace rkb {
+namespace attn {
+
+constexpr int BQ = 128, BKV = 128, DH = 64;
+constexpr int NUM_THREADS = 192;
+constexpr int Q_BYTES = BQ * DH * 2;        // 16 KB
+constexpr int K_BYTES = BKV * DH * 2;       // 16 KB
+constexpr int VT_BYTES = DH * BKV * 2;      // 16 KB (two 64-key panels of 8 KB)
+constexpr int P_BYTES = BQ * BKV * 2;       // 32 KB (two 64-key panels of 16 KB)
+constexpr int KV_STAGES = 2;
+constexpr int KV_STAGE = K_BYTES + VT_BYTES;
+constexpr int OFF_Q = 0;
+constexpr int OFF_KV = Q_BYTES;
+constexpr int OFF_P = OFF_KV + KV_STAGES * KV_STAGE;
+constexpr int OFF_BAR = OFF_P + P_BYTES;
+constexpr int NBARS = 1 + 2 * KV_STAGES + 4;
+constexpr int SMEM = OFF_BAR + NBARS * 8 + 16 + 1024;
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t S_COL = 0, O_COL = 128;
+
+struct Args {
+    int T, Tp, H, nkb;
+    float scale_log2;     // softmax scale * log2(e)
+    __half *out;
+    long ldo;
+    int *err;
+};
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+            const __grid_constant__ CUtensorMap tmVt, const Args g) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const uint32_t sb = smem_u32(smem);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBARS);
+    const uint32_t q_full = smem_u32(&bars[0]);
+    auto kv_full = [&](int s) { return smem_u32(&bars[1 + s]); };
+    auto kv_empty = [&](int s) { return smem_u32(&bars[1 + KV_STAGES + s]); };
+    const uint32_t s_full = smem_u32(&bars[1 + 2 * KV_STAGES]);
+    const uint32_t s_free = smem_u32(&bars[2 + 2 * KV_STAGES]);
+    const uint32_t p_full = smem_u32(&bars[3 + 2 * KV_STAGES]);
+    const uint32_t o_full = smem_u32(&bars[4 + 2 * KV_STAGES]);
+    auto sK = [&](int s) { return sb + OFF_KV + s * KV_STAGE; };
+    auto sVt = [&](int s) { return sb + OFF_KV + s * KV_STAGE + K_BYTES; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qt = blockIdx.x, bh = blockIdx.y;
+
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&tmQ);
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmVt);
+        mbar_init(q_full, 1);
+        for (int s = 0; s < KV_STAGES; ++s) {
+            mbar_init(kv_full(s), 1);
+            mbar_init(kv_empty(s), 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 4);
+        mbar_init(p_full, 4);
+        mbar_init(o_full, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int nkb = g.nkb;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(q_full, Q_BYTES);
+            tma_load_2d(sb + OFF_Q, &tmQ, 0, bh * g.Tp + qt * BQ, q_full);
+            for (int j = 0; j < nkb; ++j) {
+                const int s = j % KV_STAGES;
+                const uint32_t ph = (j / KV_STAGES) & 1;
+                if (!mbar_wait(kv_empty(s), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) break;
+                mbar_arrive_expect_tx(kv_full(s), KV_STAGE);
+                tma_load_2d(sK(s), &tmK, 0, bh * g.Tp + j * BKV, kv_full(s));
+                tma_load_2d(sVt(s), &tmVt, j * BKV, bh * DH, kv_full(s));
+                tma_load_2d(sVt(s) + VT_BYTES / 2, &tmVt, j * BKV + 64, bh * DH, kv_full(s));
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t IDS = idesc_f16_f32acc(BQ, BKV);
+            constexpr uint32_t IDO = idesc_f16_f32acc(BQ, DH);
+            bool ok = mbar_wait(q_full, 0, g.err, ERR_WAIT_MMA_FULL) &&
+                      mbar_wait(kv_full(0), 0, g.err, ERR_WAIT_MMA_FULL);
+            if (ok) {
+                tc_fence_after();
+                const uint64_t qd = smem_desc_sw128(sb + OFF_Q), kd = smem_desc_sw128(sK(0));
+#pragma unroll
+                for (int k = 0; k < 4; ++k) tc_mma_f16(tmem + S_COL, qd + 2 * k, kd + 2 * k, IDS, k > 0);
+                tc_commit(s_full);
+            }
+            for (int j = 0; j < nkb && ok; ++j) {
+                if (j + 1 < nkb) {
+                    const int s1 = (j + 1) % KV_STAGES;
+                    if (!mbar_wait(kv_full(s1), ((j + 1) / KV_STAGES) & 1, g.err, ERR_WAIT_MMA_FULL) ||
+                        !mbar_wait(s_free, j & 1, g.err, ERR_WAIT_MMA_ACC)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t qd = smem_desc_sw128(sb + OFF_Q), kd = smem_desc_sw128(sK(s1));
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) tc_mma_f16(tmem + S_COL, qd + 2 * k, kd + 2 * k, IDS, k > 0);
+                    tc_commit(s_full);
+                }
+                if (!mbar_wait(p_full, j & 1, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
+                tc_fence_after();
+                const int s = j % KV_STAGES;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint64_t pd = smem_desc_sw128(sb + OFF_P + (kk >> 2) * (P_BYTES / 2) + (kk & 3) * 32);
+                    const uint64_t vd = smem_desc_sw128(sVt(s) + (kk >> 2) * (VT_BYTES / 2) + (kk & 3) * 32);
+                    tc_mma_f16(tmem + O_COL, pd, vd, IDO, kk > 0);
+                }
+                tc_commit(o_full);
+                tc_commit(kv_empty(s));
+            }
+            if (!ok) {
+                tc_commit(q_full);   // drain: arrives once every issued MMA has finished
+                mbar_wait_drain(q_full, 1);
+            }
+        }
+    } else {
+        const int q4 = warp & 3;
+        const int row = q4 * 32 + lane;
+        const uint32_t tl = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+        float o[DH];
+#pragma unroll
+        for (int c = 0; c < DH; ++c) o[c] = 0.f;
+        float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+        uint8_t *prow = smem + OFF_P + row * 128;
+        bool ok = true;
+        for (int j = 0; j < nkb; ++j) {
+            if (!mbar_wait(s_full, j & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
+            tc_fence_after();
+            float sv[BKV];
+#pragma unroll
+            for (int c = 0; c < BKV; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(tl + S_COL + c, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sv[c + i] = __uint_as_float(r[i]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);
+            // online softmax in the log2 domain
+            const int kbase = j * BKV;
+            float mx = m;
+#pragma unroll
+            for (int c = 0; c < BKV; ++c) {
+                sv[c] = (kbase + c < g.T) ? sv[c] * g.scale_log2 : -INFINITY;
+                mx = fmaxf(mx, sv[c]);
+            }
+            const float alpha = exp2f(m - mx);   // m = -inf on the first block -> 0
+            float sum = 0.f;
+#pragma unroll
+            for (int c = 0; c < BKV; ++c) {
+                sv[c] = exp2f(sv[c] - mx);
+                sum += sv[c];
+            }
+            l = l * alpha + sum;
+            m = mx;
+            // fold O_{j-1}; after this the P tile and the O columns are free
+            if (j > 0) {
+                if (!mbar_wait(o_full, (j - 1) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < DH; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(tl + O_COL + c, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[c + i] = o[c + i] * alpha_prev + __uint_as_float(r[i]);
+                }
+            }
+            alpha_prev = alpha;
+            // P_j as fp16 into the swizzled [128 x 128] A tile (two 64-key panels)
+#pragma unroll
+            for (int cg = 0; cg < 16; ++cg) {
+                uint32_t h[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    __half2 p = __floats2half2_rn(sv[cg * 8 + 2 * i], sv[cg * 8 + 2 * i + 1]);
+                    h[i] = *reinterpret_cast<uint32_t *>(&p);
+                }
+                const int panel = cg >> 3, c = cg & 7;
+                *reinterpret_cast<uint4 *>(prow + panel * (P_BYTES / 2) + ((c ^ (row & 7)) << 4)) =
+                    make_uint4(h[0], h[1], h[2], h[3]);
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+        }
+        if (ok && nkb > 0 && mbar_wait(o_full, (nkb - 1) & 1, g.err, ERR_WAIT_EPILOGUE)) {
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < DH; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(tl + O_COL + c, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[c + i] = o[c + i] * alpha_prev + __uint_as_float(r[i]);
+            }
+            const int t = qt * BQ + row;
+            if (t < g.T) {
+                const int b = bh / g.H, h = bh % g.H;
+                __half *dst = g.out + static_cast<long>(b * g.T + t) * g.ldo + h * DH;
+                const float inv = 1.f / l;
+#pragma unroll
+                for (int c = 0; c < DH; c += 8) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        __half2 p = __floats2half2_rn(o[c + 2 * i] * inv, o[c + 2 * i + 1] * inv);
+                        w[i] = *reinterpret_cast<uint32_t *>(&p);
+                    }
+                    *reinterpret_cast<uint4 *>(dst + c) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+        }
+        tc_fence_before();
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+}  // namespace attn
+}  // namespace rkb
+
+extern "C" int rkb_attention(const void *Q, const void *K, const void *Vt, int B, int H, int T, int Tp,
+                             int dh, float scale, void *out, long ldo, int *err, cudaStream_t stream) {
+    using namespace rkb::attn;
+    if (dh != DH || Tp % BKV || T > Tp || T <= 0 || (ldo % 8)) return ROCKET_E_UNSUPPORTED;
+    static std::once_flag once[16];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(once[dev & 15], [] {
+        cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    });
+    CUtensorMap tq, tk, tv;
+    const long BH = static_cast<long>(B) * H;
+    if (rkb::make_tmap_2d(&tq, Q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, DH, BH * Tp, DH, 64, BQ) ||
+        rkb::make_tmap_2d(&tk, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, DH, BH * Tp, DH, 64, BKV) ||
+        rkb::make_tmap_2d(&tv, Vt, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Tp, BH * DH, Tp, 64, DH))
+        return ROCKET_E_SHAPE;
+    Args g;
+    g.T = T; g.Tp = Tp; g.H = H; g.nkb = Tp / BKV;
+    g.scale_log2 = scale * 1.4426950408889634f;
+    g.out = static_cast<__half *>(out);
+    g.ldo = ldo;
+    g.err = err;
+    dim3 grid(Tp / BQ, static_cast<unsigned>(BH));
+    attn_kernel<<<grid, NUM_THREADS, SMEM, stream>>>(tq, tk, tv, g);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        fprintf(stderr, "rkb attention launch: %s\n", cudaGetErrorString(e));
+        return ROCKET_E_DEVICE;
+    }
+    return 0;
+}

@@ -55,8 +55,18 @@ struct Args {
     long ldc;
     const float *row_scale;
     const float *col_scale;
+    const __half *bias;
+    const __half *residual;
+    long ldr;
+    int act;
     int *err;
 };
+
+RKB_DEV float apply_act(float v, int act) {
+    if (act == RKB_ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+    if (act == RKB_ACT_SILU) return v / (1.0f + expf(-v));
+    return v;
+}
 
 template <int OUT>
 RKB_DEV void store_chunk(const Args &g, int row, int col, const uint32_t (&r)[32]) {
@@ -92,19 +102,28 @@ RKB_DEV void store_chunk(const Args &g, int row, int col, const uint32_t (&r)[32
         }
     } else {
         __half *c = static_cast<__half *>(g.C) + static_cast<long>(row) * g.ldc + col;
+        const __half *res = g.residual ? g.residual + static_cast<long>(row) * g.ldr + col : nullptr;
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
             if (col + 8 * v + 8 <= g.N) {
+                float f[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float a = __uint_as_float(r[8 * v + j]) * rs;
+                    if (g.col_scale) a *= g.col_scale[col + 8 * v + j];
+                    if (g.bias) a += __half2float(g.bias[col + 8 * v + j]);
+                    f[j] = apply_act(a, g.act);
+                }
+                if (res) {
+                    const uint4 rv = *reinterpret_cast<const uint4 *>(res + 8 * v);
+                    const __half *rh = reinterpret_cast<const __half *>(&rv);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) f[j] += __half2float(rh[j]);
+                }
                 uint32_t h[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    float a = __uint_as_float(r[8 * v + 2 * j]) * rs;
-                    float b = __uint_as_float(r[8 * v + 2 * j + 1]) * rs;
-                    if (g.col_scale) {
-                        a *= g.col_scale[col + 8 * v + 2 * j];
-                        b *= g.col_scale[col + 8 * v + 2 * j + 1];
-                    }
-                    __half2 p = __floats2half2_rn(a, b);
+                    __half2 p = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
                     h[j] = *reinterpret_cast<uint32_t *>(&p);
                 }
                 *reinterpret_cast<uint4 *>(c + 8 * v) = make_uint4(h[0], h[1], h[2], h[3]);
@@ -275,6 +294,9 @@ int launch(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
     g.k_blocks = (d->K * esize + BK_BYTES - 1) / BK_BYTES;
     g.C = d->C; g.ldc = d->ldc;
     g.row_scale = d->row_scale; g.col_scale = d->col_scale;
+    g.bias = static_cast<const __half *>(d->bias);
+    g.residual = static_cast<const __half *>(d->residual);
+    g.ldr = d->ldr; g.act = d->act;
     g.err = err;
     const int tiles = g.m_tiles * g.n_tiles;
     const int sms = rkb_device_sm_count(dev);
@@ -479,6 +501,9 @@ int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
     g.k_blocks = (d->K * esize + BK_BYTES - 1) / BK_BYTES;
     g.C = d->C; g.ldc = d->ldc;
     g.row_scale = d->row_scale; g.col_scale = d->col_scale;
+    g.bias = static_cast<const __half *>(d->bias);
+    g.residual = static_cast<const __half *>(d->residual);
+    g.ldr = d->ldr; g.act = d->act;
     g.err = err;
     const int tiles = g.m_tiles * g.n_tiles;
     const int pairs = rkb_device_sm_count(dev) / 2;

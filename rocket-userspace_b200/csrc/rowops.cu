@@ -1,0 +1,291 @@
+// rowops.cu -- the HBM-bound encoder ops: LayerNorm / RMSNorm, softmax /
+// log-softmax, the activation zoo, element-wise add / mul / sub, the gated
+// product act(gate) * up, and the head split that feeds the attention kernel.
+//
+// Replaces the reference's composed NPU programs (src/rocket_norm.c:152-227,
+// src/rocket_softmax.c:38-78, src/rocket_activation.c, src/rocket_ffn.c:23-50),
+// which build each of these from LUT passes, element-wise passes and
+// ones-matmul reductions with host tails.  Here each op is one pass over HBM:
+// a warp owns a row (norms, softmax) and reduces with shuffles; element-wise
+// ops move 16 bytes per thread per step.  All arithmetic is fp32 on fp16
+// storage; reductions are exact-order independent to within fp32 rounding.
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include "../src/rkb_kernels.h"
+#include "../../include/rocket_npu.h"
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Row loads as 8-half vectors when the row is 16-byte aligned, else scalar.
+struct RowView {
+    const __half *p;
+    int n;
+    bool vec;
+};
+
+template <class F>
+__device__ __forceinline__ void row_for_each(const RowView &r, int lane, F f) {
+    if (r.vec) {
+        const int nv = r.n >> 3;
+        for (int i = lane; i < nv; i += 32) {
+            uint4 u = reinterpret_cast<const uint4 *>(r.p)[i];
+            const __half *h = reinterpret_cast<const __half *>(&u);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f(i * 8 + j, __half2float(h[j]));
+        }
+    } else {
+        for (int i = lane; i < r.n; i += 32) f(i, __half2float(r.p[i]));
+    }
+}
+
+// mode 0: LayerNorm (gamma, optional beta), mode 1: RMSNorm (weight = gamma)
+__global__ void norm_rows(const __half *__restrict__ x, const __half *__restrict__ gamma,
+                          const __half *__restrict__ beta, int M, int H, float eps, int mode,
+                          __half *__restrict__ out) {
+    const int warps = blockDim.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const bool vec = (H % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+    for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+        RowView r{x + static_cast<size_t>(row) * H, H, vec};
+        float mean = 0.f;
+        if (mode == 0) {
+            float s = 0.f;
+            row_for_each(r, lane, [&](int, float v) { s += v; });
+            mean = warp_sum(s) / H;
+        }
+        float q = 0.f;
+        row_for_each(r, lane, [&](int, float v) { const float d = v - mean; q += d * d; });
+        const float rstd = rsqrtf(warp_sum(q) / H + eps);
+        __half *o = out + static_cast<size_t>(row) * H;
+        if (vec) {
+            const int nv = H >> 3;
+            for (int i = lane; i < nv; i += 32) {
+                uint4 u = reinterpret_cast<const uint4 *>(r.p)[i];
+                uint4 g = reinterpret_cast<const uint4 *>(gamma)[i];
+                uint4 b = beta ? reinterpret_cast<const uint4 *>(beta)[i] : make_uint4(0, 0, 0, 0);
+                const __half *h = reinterpret_cast<const __half *>(&u);
+                const __half *gh = reinterpret_cast<const __half *>(&g);
+                const __half *bh = reinterpret_cast<const __half *>(&b);
+                uint4 w;
+                __half *wh = reinterpret_cast<__half *>(&w);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    wh[j] = __float2half_rn((__half2float(h[j]) - mean) * rstd * __half2float(gh[j]) +
+                                            __half2float(bh[j]));
+                reinterpret_cast<uint4 *>(o)[i] = w;
+            }
+        } else {
+            for (int i = lane; i < H; i += 32) {
+                const float b = beta ? __half2float(beta[i]) : 0.f;
+                o[i] = __float2half_rn((__half2float(r.p[i]) - mean) * rstd * __half2float(gamma[i]) + b);
+            }
+        }
+    }
+}
+
+// mode 0: softmax, mode 1: log-softmax
+__global__ void softmax_rows(const __half *__restrict__ x, int M, int N, int mode,
+                             __half *__restrict__ out) {
+    const int warps = blockDim.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const bool vec = (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+    for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+        RowView r{x + static_cast<size_t>(row) * N, N, vec};
+        float mx = -INFINITY;
+        row_for_each(r, lane, [&](int, float v) { mx = fmaxf(mx, v); });
+        mx = warp_max(mx);
+        float s = 0.f;
+        row_for_each(r, lane, [&](int, float v) { s += expf(v - mx); });
+        s = warp_sum(s);
+        const float inv = 1.f / s, lse = mx + logf(s);
+        __half *o = out + static_cast<size_t>(row) * N;
+        if (vec) {
+            const int nv = N >> 3;
+            for (int i = lane; i < nv; i += 32) {
+                uint4 u = reinterpret_cast<const uint4 *>(r.p)[i];
+                const __half *h = reinterpret_cast<const __half *>(&u);
+                uint4 w;
+                __half *wh = reinterpret_cast<__half *>(&w);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float v = __half2float(h[j]);
+                    wh[j] = __float2half_rn(mode ? v - lse : expf(v - mx) * inv);
+                }
+                reinterpret_cast<uint4 *>(o)[i] = w;
+            }
+        } else {
+            for (int i = lane; i < N; i += 32) {
+                const float v = __half2float(r.p[i]);
+                o[i] = __float2half_rn(mode ? v - lse : expf(v - mx) * inv);
+            }
+        }
+    }
+}
+
+// Activation kinds follow the reference enum (include/rocket_activation.h:48-135);
+// definitions follow its exact host evaluation (src/rocket_activation.c:48-77).
+__device__ __forceinline__ float act_eval(int kind, float x) {
+    switch (kind) {
+    case 0: return 1.f / (1.f + expf(-x));                                   // sigmoid
+    case 1: return fminf(fmaxf(x / 6.f + 0.5f, 0.f), 1.f);                   // hardsigmoid
+    case 2: return x * fminf(fmaxf(x / 6.f + 0.5f, 0.f), 1.f);               // hardswish
+    case 3: return x / (1.f + expf(-x));                                     // silu
+    case 4: return tanhf(x);
+    case 5: return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));        // gelu (erf)
+    case 7: return x > 0.f ? sqrtf(x) : 0.f;
+    case 8: return x > 0.f ? rsqrtf(x) : 0.f;
+    case 9: return x != 0.f ? 1.f / x : 0.f;
+    case 10: return expf(x);
+    case 11: return 0.5f * (1.f + erff(x * 0.70710678118654752f));           // gelu gate (Phi)
+    case 12: return x > 0.f ? x + log1pf(expf(-x)) : log1pf(expf(x));        // softplus
+    case 13: return tanhf(x > 0.f ? x + log1pf(expf(-x)) : log1pf(expf(x))); // mish gate
+    case 14: return x * tanhf(x > 0.f ? x + log1pf(expf(-x)) : log1pf(expf(x)));
+    case 15: return fabsf(x);
+    case 18: return x > 0.f ? logf(x) : 0.f;
+    default: return 0.f;
+    }
+}
+
+// op: 0 act(a), 1 a+b, 2 a*b, 3 a-b, 4 act(a)*b
+__global__ void elementwise(const __half *__restrict__ a, const __half *__restrict__ b, int op,
+                            int kind, size_t n, __half *__restrict__ out) {
+    const size_t nv = n / 8;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < nv; i += stride) {
+        uint4 ua = reinterpret_cast<const uint4 *>(a)[i];
+        uint4 ub = b ? reinterpret_cast<const uint4 *>(b)[i] : make_uint4(0, 0, 0, 0);
+        const __half *ha = reinterpret_cast<const __half *>(&ua);
+        const __half *hb = reinterpret_cast<const __half *>(&ub);
+        uint4 w;
+        __half *wh = reinterpret_cast<__half *>(&w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float x = __half2float(ha[j]), y = __half2float(hb[j]);
+            float r;
+            switch (op) {
+            case 0: r = act_eval(kind, x); break;
+            case 1: r = x + y; break;
+            case 2: r = x * y; break;
+            case 3: r = x - y; break;
+            default: r = act_eval(kind, x) * y; break;
+            }
+            wh[j] = __float2half_rn(r);
+        }
+        reinterpret_cast<uint4 *>(out)[i] = w;
+    }
+    for (size_t i = nv * 8 + blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += stride) {
+        const float x = __half2float(a[i]), y = b ? __half2float(b[i]) : 0.f;
+        float r;
+        switch (op) {
+        case 0: r = act_eval(kind, x); break;
+        case 1: r = x + y; break;
+        case 2: r = x * y; break;
+        case 3: r = x - y; break;
+        default: r = act_eval(kind, x) * y; break;
+        }
+        out[i] = __float2half_rn(r);
+    }
+}
+
+// qkv [B*T, 3d] (q | k | v column blocks) -> per head, zero-padded to Tp rows:
+//   Q [B*H, Tp, dh], K [B*H, Tp, dh], Vt [B*H, dh, Tp]
+__global__ void split_heads(const __half *__restrict__ qkv, long ld, int B, int T, int Tp, int H,
+                            int dh, __half *__restrict__ Q, __half *__restrict__ K,
+                            __half *__restrict__ Vt) {
+    // one thread per (b, h, t, 8-wide chunk of dh)
+    const int cpr = dh / 8;
+    const size_t total = static_cast<size_t>(B) * H * Tp * cpr;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % cpr);
+        const int t = static_cast<int>((i / cpr) % Tp);
+        const int bh = static_cast<int>(i / (static_cast<size_t>(cpr) * Tp));
+        const int b = bh / H, h = bh % H;
+        uint4 q = make_uint4(0, 0, 0, 0), k = q, v = q;
+        if (t < T) {
+            const __half *row = qkv + static_cast<size_t>(b * T + t) * ld + h * dh + c * 8;
+            const int d = H * dh;
+            q = *reinterpret_cast<const uint4 *>(row);
+            k = *reinterpret_cast<const uint4 *>(row + d);
+            v = *reinterpret_cast<const uint4 *>(row + 2 * d);
+        }
+        const size_t qo = (static_cast<size_t>(bh) * Tp + t) * dh + c * 8;
+        *reinterpret_cast<uint4 *>(Q + qo) = q;
+        *reinterpret_cast<uint4 *>(K + qo) = k;
+        const __half *vh = reinterpret_cast<const __half *>(&v);
+        __half *vt = Vt + static_cast<size_t>(bh) * dh * Tp;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) vt[static_cast<size_t>(c * 8 + j) * Tp + t] = vh[j];
+    }
+}
+
+int grid_for(size_t work, int threads) {
+    size_t b = (work + threads - 1) / threads;
+    if (b > 148 * 32) b = 148 * 32;
+    return b < 1 ? 1 : static_cast<int>(b);
+}
+int status() { return cudaGetLastError() == cudaSuccess ? 0 : ROCKET_E_DEVICE; }
+
+}  // namespace
+
+extern "C" {
+
+int rkb_norm_rows(const void *x, const void *gamma, const void *beta, int M, int H, float eps,
+                  int rms, void *out, cudaStream_t s) {
+    if (M <= 0 || H <= 0 || !gamma) return ROCKET_E_SHAPE;
+    const int warps = 8;
+    int grid = (M + warps - 1) / warps;
+    if (grid > 148 * 16) grid = 148 * 16;
+    norm_rows<<<grid, warps * 32, 0, s>>>(static_cast<const __half *>(x), static_cast<const __half *>(gamma),
+                                          static_cast<const __half *>(beta), M, H, eps, rms ? 1 : 0,
+                                          static_cast<__half *>(out));
+    return status();
+}
+
+int rkb_softmax_rows(const void *x, int M, int N, int log_mode, void *out, cudaStream_t s) {
+    if (M <= 0 || N <= 0) return ROCKET_E_SHAPE;
+    const int warps = 8;
+    int grid = (M + warps - 1) / warps;
+    if (grid > 148 * 16) grid = 148 * 16;
+    softmax_rows<<<grid, warps * 32, 0, s>>>(static_cast<const __half *>(x), M, N, log_mode ? 1 : 0,
+                                             static_cast<__half *>(out));
+    return status();
+}
+
+int rkb_elementwise(const void *a, const void *b, int op, int kind, size_t n, void *out,
+                    cudaStream_t s) {
+    if (n == 0) return ROCKET_E_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+         reinterpret_cast<uintptr_t>(out)) & 15)
+        return ROCKET_E_SHAPE;
+    elementwise<<<grid_for(n / 8 + 1, 256), 256, 0, s>>>(static_cast<const __half *>(a),
+                                                         static_cast<const __half *>(b), op, kind, n,
+                                                         static_cast<__half *>(out));
+    return status();
+}
+
+int rkb_split_heads(const void *qkv, long ld, int B, int T, int Tp, int H, int dh, void *Q, void *K,
+                    void *Vt, cudaStream_t s) {
+    if (dh % 8 || (ld % 8)) return ROCKET_E_SHAPE;
+    const size_t total = static_cast<size_t>(B) * H * Tp * (dh / 8);
+    split_heads<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const __half *>(qkv), ld, B, T, Tp, H, dh,
+                                                     static_cast<__half *>(Q), static_cast<__half *>(K),
+                                                     static_cast<__half *>(Vt));
+    return status();
+}
+
+}  // extern "C"

@@ -29,7 +29,7 @@ enum rkb_kfam {
     RKB_K_GEMM_I8 = 0, RKB_K_GEMM_F16, RKB_K_WGEMM_W4_F16, RKB_K_WGEMM_W8_F16, RKB_K_WGEMM_W4_I8,
     RKB_K_PACK, RKB_K_PRESCALE, RKB_K_NORM, RKB_K_SOFTMAX, RKB_K_ATTN, RKB_K_ELEMWISE, RKB_NKFAM
 };
-#define RKB_PROF_SLOTS 64
+#define RKB_PROF_SLOTS 4096
 
 typedef struct rkb_handle {
     int in_use;
@@ -75,6 +75,9 @@ int rkb_finish(rkb_handle *h, const char *who);
  * end records the closing event for kernel family `fam`. */
 int  rkb_prof_begin(rkb_handle *h);
 void rkb_prof_end(rkb_handle *h, int slot, int fam);
+
+/* Deferred completion requested by this host thread (rocket_b200_set_async). */
+int  rkb_async_enabled(void);
 
 /* Count one device-reaching call and the kernels it launched. */
 void rkb_count(uint64_t calls, uint64_t kernels);

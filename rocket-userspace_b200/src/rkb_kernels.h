@@ -31,7 +31,15 @@ typedef struct {
     void *C; long ldc;
     const float *row_scale;
     const float *col_scale;
+    /* fp16-output epilogue extras (ignored for int32 output):
+     *   out = act(acc * row_scale * col_scale + bias[n]) + residual[m * ldr + n] */
+    const void *bias;          /* fp16 [N] or NULL */
+    int act;                   /* RKB_ACT_* */
+    const void *residual;      /* fp16, or NULL */
+    long ldr;
 } rkb_gemm_desc;
+
+enum rkb_act { RKB_ACT_NONE = 0, RKB_ACT_GELU = 1, RKB_ACT_SILU = 2 };
 
 int rkb_gemm_run(const rkb_gemm_desc *d, int *err_word, cudaStream_t stream);
 
@@ -72,6 +80,20 @@ int rkb_prescale_a(const int8_t *A, const float *a_scale, int M, int K, int grou
 /* Rows of a_scale [M, nG] all constant?  Host-side check result is passed in
  * by the caller; this only gathers a_scale[m*nG] into a dense [M] vector. */
 int rkb_gather_row_scale(const float *a_scale, int M, int nG, float *dst, cudaStream_t s);
+
+/* ---- encoder ops (csrc/rowops.cu, csrc/attn_tc.cu); fp16 storage ---- */
+int rkb_norm_rows(const void *x, const void *gamma, const void *beta, int M, int H, float eps,
+                  int rms, void *out, cudaStream_t s);
+int rkb_softmax_rows(const void *x, int M, int N, int log_mode, void *out, cudaStream_t s);
+/* op: 0 act(a), 1 a+b, 2 a*b, 3 a-b, 4 act(a)*b; kind = rocket_activation_kind */
+int rkb_elementwise(const void *a, const void *b, int op, int kind, size_t n, void *out,
+                    cudaStream_t s);
+/* qkv [B*T, 3*H*dh] (row pitch ld) -> Q, K [B*H, Tp, dh], Vt [B*H, dh, Tp], zero padded */
+int rkb_split_heads(const void *qkv, long ld, int B, int T, int Tp, int H, int dh, void *Q,
+                    void *K, void *Vt, cudaStream_t s);
+/* out[b*T + t, h*dh + c] = softmax(Q K^T * scale) V per (b, h); dh == 64, Tp % 128 == 0 */
+int rkb_attention(const void *Q, const void *K, const void *Vt, int B, int H, int T, int Tp,
+                  int dh, float scale, void *out, long ldo, int *err, cudaStream_t stream);
 
 /* Device properties cached per device. */
 int rkb_device_sm_count(int dev);

@@ -102,6 +102,17 @@ static void prof_drain(rkb_handle *h)
     h->ev_used = 0;
 }
 
+static __thread int g_async;
+void rocket_b200_set_async(int on) { g_async = on ? 1 : 0; }
+int  rkb_async_enabled(void) { return g_async; }
+
+int rocket_b200_sync(int fd)
+{
+    rkb_handle *h = rkb_get(fd);
+    if (!h) return ROCKET_E_DEVICE;
+    return rkb_finish(h, "rocket_b200_sync");
+}
+
 void *rocket_b200_stream(int fd)
 {
     rkb_handle *h = rkb_get(fd);

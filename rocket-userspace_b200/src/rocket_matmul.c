@@ -141,6 +141,7 @@ static int oneshot_dense(const char *who, int fd, int in_kind, int out_kind, int
     int rc = rkb_dense_on(h, in_kind, out_kind, M, N, K, dA, K, dB, K, dC, N);
     if (!rc) rc = rkb_stage_out_finish(h, C, dC, (size_t)M * N * osz, cb);
     rkb_count(1, 0);
+    if (!rc && rkb_async_enabled() && dA == A && dB == B && !cb) return 0;   /* deferred */
     int fr = rkb_finish(h, who);
     return rc ? rc : fr;
 }

@@ -194,17 +194,20 @@ static int rrun(const rkb_rctx *c, const rkb_rweights *w, int M, const rrun_args
     if (w->kind == RW_I8_GW || w->kind == RW_I4_GW)
         rows_const = rkb_ptr_device(a->a_scale) < 0 ? rkb_rows_const(a->a_scale, M, K / w->group) : 0;
     int rc = 0;
+    int staged = 0;
     for (int t = 0; t < w->nt && !rc; t++) {
         const int n0 = w->n0[t], nsub = w->nsub[t];
         if (nsub <= 0) continue;
         rkb_handle *h = rkb_get(c->fd[t]);
         const void *dA = rkb_stage_in(h, RKB_SCR_A, a->A, (size_t)M * K * esz);
         if (!dA) { rc = ROCKET_E_NOMEM; break; }
+        if (dA != a->A) staged = 1;
         /* write straight into C when it lives on this GPU, else into scratch */
         uint8_t *cslice = (uint8_t *)a->C + (size_t)n0 * osz;
         const int direct = (c_dev == h->device) && (((uintptr_t)cslice & 15) == 0);
         void *dC = direct ? (void *)cslice : rkb_scratch(h, RKB_SCR_C, (size_t)M * nsub * osz);
         const long ldc = direct ? N : nsub;
+        if (!direct) staged = 1;
         if (!dC) { rc = ROCKET_E_NOMEM; break; }
         switch (w->kind) {
         case RW_F16:
@@ -241,9 +244,26 @@ static int rrun(const rkb_rctx *c, const rkb_rweights *w, int M, const rrun_args
         }
         rkb_count(1, 0);
     }
+    /* Deferred completion (rocket_b200_set_async): with every operand already
+     * on the workers' GPUs nothing host-visible is pending, so the call can
+     * return after the launches; rocket_b200_ctx_sync collects the status. */
+    const int gw = (w->kind == RW_I8_GW || w->kind == RW_I4_GW);
+    if (!rc && rkb_async_enabled() && !staged && !gw) return 0;
     for (int t = 0; t < w->nt; t++) {
         if (w->nsub[t] <= 0) continue;
         int fr = rkb_finish(rkb_get(c->fd[t]), who);
+        if (!rc) rc = fr;
+    }
+    return rc;
+}
+
+int rocket_b200_ctx_sync(const void *ctx)
+{
+    const rkb_rctx *c = ctx;
+    if (!c) return ROCKET_E_SHAPE;
+    int rc = 0;
+    for (int t = 0; t < c->nthreads; t++) {
+        int fr = rkb_finish(rkb_get(c->fd[t]), "rocket_b200_ctx_sync");
         if (!rc) rc = fr;
     }
     return rc;

@@ -154,3 +154,29 @@ def test_bo_roundtrip(rkb, dev):
     assert rkb.lib.rocket_bo_prep(dev.fd, ctypes.byref(bo), 0, 2_000_000_000) == 0
     assert all(buf[i] == (i & 0xFF) for i in range(0, bo.size, 97))
     rkb.lib.rocket_bo_free(dev.fd, ctypes.byref(bo))
+
+
+def test_async_enqueue_then_sync(rkb, dev, orc):
+    """rocket_b200_set_async: device-resident resident calls queue without
+    waiting; rocket_b200_ctx_sync returns their status; results unchanged."""
+    import torch
+    M, K, N = 256, 1024, 512
+    ctx = rkb.lib.rocket_i8_ctx_create(1)
+    A = orc.uniform_i8(61, -128, 127, (M, K))
+    Bs = [orc.uniform_i8(62 + i, -128, 127, (N, K)) for i in range(3)]
+    ws = [rkb.lib.rocket_i8_weights_pack(ctx, M, K, N, rkb.ptr(B)) for B in Bs]
+    dA = torch.from_numpy(A).cuda()
+    Cs = [torch.full((M, N), 7, dtype=torch.int32, device="cuda") for _ in Bs]
+    rkb.lib.rocket_b200_set_async(1)
+    try:
+        for _ in range(3):
+            for w, C in zip(ws, Cs):
+                assert rkb.lib.rocket_matmul_int8_prepacked(ctx, M, K, N, rkb.ptr(dA), rkb.ptr(C), w) == 0
+        assert rkb.lib.rocket_b200_ctx_sync(ctx) == 0
+    finally:
+        rkb.lib.rocket_b200_set_async(0)
+    for B, C in zip(Bs, Cs):
+        assert np.array_equal(C.cpu().numpy(), orc.matmul_int8(A, B, nthreads=8))
+    for w in ws:
+        rkb.lib.rocket_i8_weights_free(ctx, w)
+    rkb.lib.rocket_i8_ctx_free(ctx)
