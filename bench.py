@@ -332,7 +332,8 @@ def main_ours(args):
     # ---- other configs (rank 0, N=1 only)
     others = None
     if world == 1 and not args.no_extra:
-        others = other_configs(rkb, torch, peaks, derived_peak)
+        others = other_configs(rkb, torch, peaks, derived_peak,
+                               tuple(args.side.split(",")) if args.side else ("c1", "c2", "c3", "c4"))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -360,7 +361,7 @@ def main_ours(args):
     return 0
 
 
-def other_configs(rkb, torch, peaks, derived_i8_peak):
+def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "c4")):
     """fp16 (config 2), W4A8 group-wise (config 3) and int8 latency (config 1)."""
     L = rkb.lib
     out = {}
@@ -380,82 +381,133 @@ def other_configs(rkb, torch, peaks, derived_i8_peak):
         return a.elapsed_time(b) / n
 
     # config 2: fp16 512x4096x4096
-    M, K, N = 512, 4096, 4096
-    A = (torch.randn((M, K), device="cuda") / K ** 0.5).half()
-    B = (torch.randn((N, K), device="cuda") / K ** 0.5).half()
-    C = torch.empty((M, N), dtype=torch.float16, device="cuda")
-    ms = timed(lambda: dev.matmul_fp16(M, K, N, A, B, C), 50)
-    ref = torch.matmul(A, B.t())
-    t = timed(lambda: torch.matmul(A, B.t()), 50)
-    out["config2_fp16"] = {"tflops": 2 * M * N * K / ms / 1e9, "ms": ms,
-                           "frac_of_measured_bf16": 2 * M * N * K / ms / 1e9 / peaks["bf16_tflops"],
-                           "torch_cublas_tflops": 2 * M * N * K / t / 1e9,
-                           "rel_fro_vs_cublas": float((C.float() - ref.float()).norm() / ref.float().norm())}
-    # large fp16 for the kernel's steady-state rate
-    M2 = 4096
-    A2 = torch.randn((M2, K), device="cuda").half()
-    C2 = torch.empty((M2, N), dtype=torch.float16, device="cuda")
-    ms2 = timed(lambda: dev.matmul_fp16(M2, K, N, A2, B, C2), 30)
-    out["fp16_4096x4096x4096"] = {"tflops": 2 * M2 * N * K / ms2 / 1e9,
-                                  "frac_of_measured_bf16": 2 * M2 * N * K / ms2 / 1e9 / peaks["bf16_tflops"]}
-    del A2, C2
+    if "c2" in which:
+        M, K, N = 512, 4096, 4096
+        A = (torch.randn((M, K), device="cuda") / K ** 0.5).half()
+        B = (torch.randn((N, K), device="cuda") / K ** 0.5).half()
+        C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        ms = timed(lambda: dev.matmul_fp16(M, K, N, A, B, C), 50)
+        ref = torch.matmul(A, B.t())
+        t = timed(lambda: torch.matmul(A, B.t()), 50)
+        out["config2_fp16"] = {"tflops": 2 * M * N * K / ms / 1e9, "ms": ms,
+                               "frac_of_measured_bf16": 2 * M * N * K / ms / 1e9 / peaks["bf16_tflops"],
+                               "torch_cublas_tflops": 2 * M * N * K / t / 1e9,
+                               "rel_fro_vs_cublas": float((C.float() - ref.float()).norm() / ref.float().norm())}
+        # large fp16 for the kernel's steady-state rate
+        M2 = 4096
+        A2 = torch.randn((M2, K), device="cuda").half()
+        C2 = torch.empty((M2, N), dtype=torch.float16, device="cuda")
+        ms2 = timed(lambda: dev.matmul_fp16(M2, K, N, A2, B, C2), 30)
+        out["fp16_4096x4096x4096"] = {"tflops": 2 * M2 * N * K / ms2 / 1e9,
+                                      "frac_of_measured_bf16": 2 * M2 * N * K / ms2 / 1e9 / peaks["bf16_tflops"]}
+        del A2, C2
 
     # config 3: W4A8 group-wise resident 2048x3840x15360, group 32
-    M, K, N, gsz = 2048, 3840, 15360, 32
-    nG = K // gsz
-    ctx = L.rocket_i4_ctx_create(1)
-    Wt = torch.randint(-8, 8, (N, K), dtype=torch.int8, device="cuda")
-    w = L.rocket_i4_weights_pack_gw(ctx, M, K, N, Wt.data_ptr(), gsz)
-    Aq = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
-    asc = (torch.rand((M, 1), device="cuda") * 0.04 + 0.01).expand(M, nG).contiguous()
-    bsc = torch.rand((N, nG), device="cuda") * 0.015 + 0.005
-    Cf = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    fd3 = L.rocket_b200_ctx_fd(ctx, 0)
-    s3 = torch.cuda.ExternalStream(L.rocket_b200_stream(fd3))
-    run3 = lambda: L.rocket_matmul_int4_prepacked_gw(ctx, M, K, N, Aq.data_ptr(), asc.data_ptr(),
-                                                     bsc.data_ptr(), Cf.data_ptr(), w)
-    for _ in range(3):
-        run3()
-    torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    L.rocket_b200_profile_reset()
-    L.rocket_b200_profile_enable(1)
-    a.record(s3)
-    for _ in range(20):
-        run3()
-    b.record(s3)
-    torch.cuda.synchronize()
-    L.rocket_b200_profile_enable(0)
-    ms3 = a.elapsed_time(b) / 20
-    prof = rkb.profile_snapshot()
-    nk, kms = prof.get("wgemm_w4_f16_tcgen05", (1, 0.0))
-    out["config3_w4a8_gw"] = {"tops_call": 2 * M * N * K / ms3 / 1e9, "ms_call": ms3,
+    if "c3" in which:
+        M, K, N, gsz = 2048, 3840, 15360, 32
+        nG = K // gsz
+        ctx = L.rocket_i4_ctx_create(1)
+        Wt = torch.randint(-8, 8, (N, K), dtype=torch.int8, device="cuda")
+        w = L.rocket_i4_weights_pack_gw(ctx, M, K, N, Wt.data_ptr(), gsz)
+        Aq = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+        asc = (torch.rand((M, 1), device="cuda") * 0.04 + 0.01).expand(M, nG).contiguous()
+        bsc = torch.rand((N, nG), device="cuda") * 0.015 + 0.005
+        Cf = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        fd3 = L.rocket_b200_ctx_fd(ctx, 0)
+        s3 = torch.cuda.ExternalStream(L.rocket_b200_stream(fd3))
+        run3 = lambda: L.rocket_matmul_int4_prepacked_gw(ctx, M, K, N, Aq.data_ptr(), asc.data_ptr(),
+                                                         bsc.data_ptr(), Cf.data_ptr(), w)
+        for _ in range(3):
+            run3()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        L.rocket_b200_profile_reset()
+        L.rocket_b200_profile_enable(1)
+        a.record(s3)
+        for _ in range(20):
+            run3()
+        b.record(s3)
+        torch.cuda.synchronize()
+        L.rocket_b200_profile_enable(0)
+        ms3 = a.elapsed_time(b) / 20
+        prof = rkb.profile_snapshot()
+        nk, kms = prof.get("wgemm_w4_f16_tcgen05", (1, 0.0))
+        out["config3_w4a8_gw"] = {"tops_call": 2 * M * N * K / ms3 / 1e9, "ms_call": ms3,
                               "kernel_tops": 2 * M * N * K / (kms / max(nk, 1)) / 1e9,
                               "kernel_frac_of_measured_f16": 2 * M * N * K / (kms / max(nk, 1)) / 1e9 / peaks["bf16_tflops"],
                               "per_call_kernels": {k: v for k, v in prof.items() if v[0]},
                               "note": "fp16 MMA after in-register int4 dequant: peak is the fp16 dense rate"}
-    L.rocket_i4_weights_free(ctx, w)
-    L.rocket_i4_ctx_free(ctx)
+        L.rocket_i4_weights_free(ctx, w)
+        L.rocket_i4_ctx_free(ctx)
+
+    # config 4: encoder block fp16, d=512, 8 heads, T=1500, batch 4 (batched extension)
+    if "c4" in which:
+        nb, T, d, nh, dff = 4, 1500, 512, 8, 2048
+        BT = nb * T
+        gq = torch.Generator(device="cuda")
+        gq.manual_seed(4)
+        pw = {}
+        for k, shp in [("Wq", (d, d)), ("Wk", (d, d)), ("Wv", (d, d)), ("Wo", (d, d)), ("W1", (dff, d)), ("W2", (d, dff))]:
+            pw[k] = (torch.randn(shp, device="cuda", generator=gq) * 0.02).half()
+        for k, n in [("bq", d), ("bk", d), ("bv", d), ("bo", d), ("b1", dff), ("b2", d)]:
+            pw[k] = (torch.randn(n, device="cuda", generator=gq) * 0.02).half()
+        for k in ("ln1_g", "ln2_g"):
+            pw[k] = torch.ones(d, device="cuda", dtype=torch.float16)
+        for k in ("ln1_b", "ln2_b"):
+            pw[k] = torch.zeros(d, device="cuda", dtype=torch.float16)
+        xe = torch.randn((BT, d), device="cuda", generator=gq).half()
+        ye = torch.empty_like(xe)
+        run4 = lambda: L.rocket_b200_encoder_block_batched_fp16(dev.fd, nb, T, d, nh, dff, xe.data_ptr(),
+                                                                *[pw[k].data_ptr() for k in rkb.ENCODER_KEYS],
+                                                                1e-5, ye.data_ptr())
+        flops4 = (2.0 * BT * d * 3 * d + 2.0 * BT * d * d + 2 * 2.0 * nb * nh * T * T * (d // nh)
+                  + 2 * 2.0 * BT * d * dff)
+        for _ in range(3):
+            assert run4() == 0
+        torch.cuda.synchronize()
+        L.rocket_b200_profile_reset()
+        L.rocket_b200_profile_enable(1)
+        a.record(stream)
+        for _ in range(10):
+            run4()
+        b.record(stream)
+        torch.cuda.synchronize()
+        L.rocket_b200_profile_enable(0)
+        ms4 = a.elapsed_time(b) / 10
+        prof = rkb.profile_snapshot()
+        n_ln, ms_ln = prof.get("norm", (1, 0.0))
+        ln_bytes = 2.0 * BT * d * 2 + 2 * d * 2
+        n_at, ms_at = prof.get("attention", (1, 0.0))
+        at_flops = 2 * 2.0 * nb * nh * T * T * (d // nh)
+        out["config4_encoder_block"] = {
+            "tflops": flops4 / ms4 / 1e9, "ms": ms4, "gflop": flops4 / 1e9,
+            "layernorm_gbs": ln_bytes / (ms_ln / max(n_ln, 1) / 1e3) / 1e9,
+            "layernorm_frac_of_measured_hbm": ln_bytes / (ms_ln / max(n_ln, 1) / 1e3) / 1e9 / peaks["hbm_gbs"],
+            "attention_tflops": at_flops / (ms_at / max(n_at, 1) / 1e3) / 1e12,
+            "per_kernel_ms": {k: v[1] / 10 for k, v in prof.items() if v[0]},
+            "note": "batched over 4 sequences via rocket_b200_encoder_block_batched_fp16"}
 
     # config 1: int8 64x512x256 one-shot (latency)
-    import numpy as np
-    A = np.random.default_rng(0).integers(-128, 128, (64, 512), dtype=np.int8)
-    B = np.random.default_rng(1).integers(-128, 128, (256, 512), dtype=np.int8)
-    C = np.zeros((64, 256), np.int32)
-    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
-    dC = torch.empty((64, 256), dtype=torch.int32, device="cuda")
-    t0 = time.perf_counter()
-    for _ in range(200):
-        dev.matmul_int8(64, 512, 256, dA, dB, dC)
-    dev_us = (time.perf_counter() - t0) / 200 * 1e6
-    t0 = time.perf_counter()
-    for _ in range(200):
-        dev.matmul_int8(64, 512, 256, A, B, C)
-    host_us = (time.perf_counter() - t0) / 200 * 1e6
-    exact = bool((C == (A.astype(np.int64) @ B.astype(np.int64).T).astype(np.int32)).all())
-    out["config1_int8_latency"] = {"us_per_call_device_ptrs": dev_us, "us_per_call_host_ptrs": host_us,
-                                   "bit_exact": exact,
-                                   "note": "16.8 MOP: latency-bound, TOPS not meaningful"}
+    if "c1" in which:
+        import numpy as np
+        A = np.random.default_rng(0).integers(-128, 128, (64, 512), dtype=np.int8)
+        B = np.random.default_rng(1).integers(-128, 128, (256, 512), dtype=np.int8)
+        C = np.zeros((64, 256), np.int32)
+        dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+        dC = torch.empty((64, 256), dtype=torch.int32, device="cuda")
+        t0 = time.perf_counter()
+        for _ in range(200):
+            dev.matmul_int8(64, 512, 256, dA, dB, dC)
+        dev_us = (time.perf_counter() - t0) / 200 * 1e6
+        t0 = time.perf_counter()
+        for _ in range(200):
+            dev.matmul_int8(64, 512, 256, A, B, C)
+        host_us = (time.perf_counter() - t0) / 200 * 1e6
+        exact = bool((C == (A.astype(np.int64) @ B.astype(np.int64).T).astype(np.int32)).all())
+        out["config1_int8_latency"] = {"us_per_call_device_ptrs": dev_us, "us_per_call_host_ptrs": host_us,
+                                       "bit_exact": exact,
+                                       "note": "16.8 MOP: latency-bound, TOPS not meaningful"}
     dev.close()
     return out
 
@@ -469,12 +521,23 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true")
+    ap.add_argument("--side", default="", help="comma list of side configs to run (c1,c2,c3,c4)")
+    ap.add_argument("--side-only", action="store_true", help="run only the side configs (profiling)")
     ap.add_argument("--layers", default="", help="comma list of GEMMs to run (profiling); default all four")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.side_only:
+        import torch
+        torch.cuda.set_device(0)
+        rkb = load_pkg()
+        peaks, _ = load_peaks()
+        res = other_configs(rkb, torch, peaks, 2.0 * peaks.get("bf16_tflops", 1590.0),
+                            tuple(args.side.split(",")) if args.side else ("c1", "c2", "c3", "c4"))
+        print(json.dumps({"side_configs": res}), flush=True)
+        return 0
     return main_ours(args)
 
 
