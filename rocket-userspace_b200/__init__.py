@@ -154,6 +154,8 @@ def _load():
 
 lib = _load()
 
+from . import shard  # noqa: E402  (N-column sharding across ranks)
+
 
 def declared_symbols() -> list[str]:
     return [n for n, _, _ in _SIGS]

@@ -78,6 +78,17 @@ RKB_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int *err, int code) {
         }
     }
 }
+// Warp-wide wait with one polling lane: lane 0 waits (acquire), then the warp
+// converges at __syncwarp, which orders lane 0's observation before every
+// lane's later accesses.  Keeps 31 lanes off the barrier's shared-memory word.
+// Returns the same value in every lane.
+RKB_DEV bool mbar_wait_warp(uint32_t bar, uint32_t parity, int *err, int code) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, code) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok != 0;
+}
 // Bounded wait that ignores the error word (used to drain in-flight async work
 // on an error path).  Returns false on expiry.
 RKB_DEV bool mbar_wait_drain(uint32_t bar, uint32_t parity) {

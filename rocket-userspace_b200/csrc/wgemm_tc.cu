@@ -32,6 +32,8 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <mutex>
+#include <cmath>
+#include <cstdlib>
 
 #include "rkb_ptx.cuh"
 #include "rkb_tmap.h"
@@ -44,21 +46,27 @@ namespace wq {
 constexpr int BM = 128, BN = 256;
 constexpr int NUM_THREADS = 448;
 constexpr int DEQ_WARP0 = 6, DEQ_WARPS = 8, DEQ_THREADS = DEQ_WARPS * 32;
-constexpr int STAGES = 3;
 constexpr int MODE_F16 = 0, MODE_I8 = 1;
 
 template <int MODE, int WBITS>
 struct Cfg {
+    // raw ring: A tile + code block(s) + scale block, loaded DEPTH stages ahead;
+    // dequantised ring: two 256 x 128-byte swizzled B tiles.
     static constexpr int A_BYTES = BM * 128;
-    static constexpr int D_BYTES = BN * 128;                               // dequantised B
+    static constexpr int D_BYTES = BN * 128;
     static constexpr int CODE_BLOCK = BN * 64 * WBITS / 8;                 // one 64-wide K block
     static constexpr int CODE_BYTES = (MODE == MODE_F16) ? CODE_BLOCK : 2 * CODE_BLOCK;
     static constexpr int SCALE_BYTES = (MODE == MODE_F16) ? BN * 2 * 2 : 0;
-    static constexpr int STAGE_BYTES = A_BYTES + D_BYTES + CODE_BYTES + SCALE_BYTES;
+    static constexpr int RAW_BYTES = (A_BYTES + CODE_BYTES + SCALE_BYTES + 1023) / 1024 * 1024;
     static constexpr int TX_BYTES = A_BYTES + CODE_BYTES + SCALE_BYTES;
-    static constexpr int BAR_BYTES = (3 * STAGES + 5) * 8 + 16;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-    static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment");
+    static constexpr int DSTAGES = 2;
+    static constexpr int BUDGET = 226 * 1024;
+    static constexpr int RSTAGES_FIT = (BUDGET - DSTAGES * D_BYTES - 1024 - 512) / RAW_BYTES;
+    static constexpr int RSTAGES = RSTAGES_FIT > 6 ? 6 : RSTAGES_FIT;
+    static constexpr int NBARS = 2 * RSTAGES + 2 * DSTAGES + 5;
+    static constexpr int SMEM = RSTAGES * RAW_BYTES + DSTAGES * D_BYTES + NBARS * 8 + 16 + 1024;
+    static_assert(RSTAGES >= 3, "raw ring too shallow");
+    static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 struct Args {
@@ -172,44 +180,47 @@ template <int MODE, int WBITS, int OUT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 wgemm_kernel(const __grid_constant__ CUtensorMap tmA, const Args g) {
     using C = Cfg<MODE, WBITS>;
+    constexpr int RS = C::RSTAGES, DS = C::DSTAGES;
     constexpr uint32_t IDESC = (MODE == MODE_F16) ? idesc_f16_f32acc(BM, BN) : idesc_s8_s32acc(BM, BN);
     constexpr int A_BK_ELEMS = (MODE == MODE_F16) ? 64 : 128;
-    constexpr int KB64_PER_STEP = (MODE == MODE_F16) ? 1 : 2;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * STAGES + 5);
+    // layout: [DS dequantised B tiles][RS raw stages][barriers]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + DS * C::D_BYTES + RS * C::RAW_BYTES);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NBARS);
     const uint32_t sbase = smem_u32(smem);
-    auto sA = [&](int s) { return sbase + s * C::STAGE_BYTES; };
-    auto sD = [&](int s) { return sbase + s * C::STAGE_BYTES + C::A_BYTES; };
-    auto sCode = [&](int s) { return sbase + s * C::STAGE_BYTES + C::A_BYTES + C::D_BYTES; };
-    auto sScale = [&](int s) {
-        return sbase + s * C::STAGE_BYTES + C::A_BYTES + C::D_BYTES + C::CODE_BYTES;
+    auto sD = [&](int d) { return sbase + d * C::D_BYTES; };
+    auto pD = [&](int d) { return smem + d * C::D_BYTES; };
+    auto rbase = [&](int r) { return DS * C::D_BYTES + r * C::RAW_BYTES; };
+    auto sA = [&](int r) { return sbase + rbase(r); };
+    auto sCode = [&](int r) { return sbase + rbase(r) + C::A_BYTES; };
+    auto sScale = [&](int r) { return sbase + rbase(r) + C::A_BYTES + C::CODE_BYTES; };
+    auto pCode = [&](int r) { return smem + rbase(r) + C::A_BYTES; };
+    auto pScale = [&](int r) {
+        return reinterpret_cast<const uint16_t *>(smem + rbase(r) + C::A_BYTES + C::CODE_BYTES);
     };
-    auto pCode = [&](int s) { return smem + s * C::STAGE_BYTES + C::A_BYTES + C::D_BYTES; };
-    auto pD = [&](int s) { return smem + s * C::STAGE_BYTES + C::A_BYTES; };
-    auto pScale = [&](int s) {
-        return reinterpret_cast<const uint16_t *>(smem + s * C::STAGE_BYTES + C::A_BYTES +
-                                                  C::D_BYTES + C::CODE_BYTES);
-    };
-    auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
-    auto deq_bar = [&](int s) { return smem_u32(&bars[STAGES + s]); };
-    auto empty_bar = [&](int s) { return smem_u32(&bars[2 * STAGES + s]); };
-    auto tfull_bar = [&](int b) { return smem_u32(&bars[3 * STAGES + b]); };
-    auto tempty_bar = [&](int b) { return smem_u32(&bars[3 * STAGES + 2 + b]); };
-    const uint32_t drain_bar = smem_u32(&bars[3 * STAGES + 4]);
+    auto raw_full = [&](int r) { return smem_u32(&bars[r]); };
+    auto raw_empty = [&](int r) { return smem_u32(&bars[RS + r]); };
+    auto deq_full = [&](int d) { return smem_u32(&bars[2 * RS + d]); };
+    auto deq_empty = [&](int d) { return smem_u32(&bars[2 * RS + DS + d]); };
+    auto tfull_bar = [&](int b) { return smem_u32(&bars[2 * RS + 2 * DS + b]); };
+    auto tempty_bar = [&](int b) { return smem_u32(&bars[2 * RS + 2 * DS + 2 + b]); };
+    const uint32_t drain_bar = smem_u32(&bars[2 * RS + 2 * DS + 4]);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
         prefetch_tmap(&tmA);
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(full_bar(s), 1);
-            mbar_init(deq_bar(s), DEQ_WARPS);
-            mbar_init(empty_bar(s), 1);
+        for (int r = 0; r < RS; ++r) {
+            mbar_init(raw_full(r), 1);
+            mbar_init(raw_empty(r), 1);
+        }
+        for (int d = 0; d < DS; ++d) {
+            mbar_init(deq_full(d), DEQ_WARPS);
+            mbar_init(deq_empty(d), 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull_bar(b), 1);
@@ -230,7 +241,7 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tmA, const Args g) {
 
     if (warp == 0) {
         if (lane == 0) {
-            int s = 0;
+            int r = 0;
             uint32_t ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -240,22 +251,22 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tmA, const Args g) {
                 const __half *tile_scales =
                     g.scales + static_cast<size_t>(nt) * g.kb64_total * (BN * 2);
                 for (int kb = 0; kb < g.k_blocks; ++kb) {
-                    if (!mbar_wait(empty_bar(s), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) { ok = false; break; }
-                    mbar_arrive_expect_tx(full_bar(s), C::TX_BYTES);
-                    tma_load_2d(sA(s), &tmA, kb * A_BK_ELEMS, mt * BM, full_bar(s));
-                    bulk_load(sCode(s), tile_codes + static_cast<size_t>(kb) * C::CODE_BYTES,
-                              C::CODE_BYTES, full_bar(s));
+                    if (!mbar_wait(raw_empty(r), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) { ok = false; break; }
+                    mbar_arrive_expect_tx(raw_full(r), C::TX_BYTES);
+                    tma_load_2d(sA(r), &tmA, kb * A_BK_ELEMS, mt * BM, raw_full(r));
+                    bulk_load(sCode(r), tile_codes + static_cast<size_t>(kb) * C::CODE_BYTES,
+                              C::CODE_BYTES, raw_full(r));
                     if (MODE == MODE_F16)
-                        bulk_load(sScale(s), tile_scales + static_cast<size_t>(kb) * (BN * 2),
-                                  C::SCALE_BYTES, full_bar(s));
-                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                        bulk_load(sScale(r), tile_scales + static_cast<size_t>(kb) * (BN * 2),
+                                  C::SCALE_BYTES, raw_full(r));
+                    if (++r == RS) { r = 0; ph ^= 1; }
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            int s = 0;
-            uint32_t ph = 0;
+            int r = 0, d = 0;
+            uint32_t rph = 0, dph = 0;
             bool ok = true;
             int it = 0;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
@@ -265,10 +276,12 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tmA, const Args g) {
                 tc_fence_after();
                 const uint32_t dcol = tmem_base + b * BN;
                 for (int kb = 0; kb < g.k_blocks; ++kb) {
-                    if (!mbar_wait(deq_bar(s), ph, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
+                    // deq_full(d) completes only after the dequantisers saw raw_full(r),
+                    // so the A tile of raw stage r has landed as well
+                    if (!mbar_wait(deq_full(d), dph, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
                     tc_fence_after();
-                    const uint64_t adesc = smem_desc_sw128(sA(s));
-                    const uint64_t bdesc = smem_desc_sw128(sD(s));
+                    const uint64_t adesc = smem_desc_sw128(sA(r));
+                    const uint64_t bdesc = smem_desc_sw128(sD(d));
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
                         const uint64_t koff = static_cast<uint64_t>((k * 32) >> 4);
@@ -276,11 +289,14 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tmA, const Args g) {
                         if (MODE == MODE_F16) tc_mma_f16(dcol, adesc + koff, bdesc + koff, IDESC, acc);
                         else                  tc_mma_i8(dcol, adesc + koff, bdesc + koff, IDESC, acc);
                     }
-                    tc_commit(empty_bar(s));
-                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                    tc_commit(raw_empty(r));
+                    tc_commit(deq_empty(d));
+                    if (++r == RS) { r = 0; rph ^= 1; }
+                    if (++d == DS) { d = 0; dph ^= 1; }
                 }
                 if (ok) tc_commit(tfull_bar(b));
             }
+            (void)rph;
             if (!ok) {
                 tc_commit(drain_bar);
                 mbar_wait_drain(drain_bar, 0);
@@ -292,42 +308,43 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tmA, const Args g) {
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
             const int b = it & 1;
             const uint32_t aph = (it >> 1) & 1;
-            if (!mbar_wait(tfull_bar(b), aph, g.err, ERR_WAIT_EPILOGUE)) break;
+            if (!mbar_wait_warp(tfull_bar(b), aph, g.err, ERR_WAIT_EPILOGUE)) break;
             tc_fence_after();
             const int mt = t % g.m_tiles, nt = t / g.m_tiles;
             const int row = mt * BM + q * 32 + lane;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
-                uint32_t r[32];
-                tmem_ld32(tbase + c, r);
+                uint32_t rr[32];
+                tmem_ld32(tbase + c, rr);
                 tmem_ld_wait();
                 const int col = nt * BN + c;
-                if (col < g.N) store_chunk<OUT>(g, row, col, r);
+                if (col < g.N) store_chunk<OUT>(g, row, col, rr);
             }
             tc_fence_before();
             mbar_arrive(tempty_bar(b));
         }
     } else {
-        // Dequantisers: 256 threads turn one raw stage into a 256 x 128-byte
-        // swizzled operand tile.  Chunk id = i * 256 + tid covers (row, 16-byte
-        // chunk c); the swizzled destination is row * 128 + ((c ^ (row & 7)) << 4).
+        // Dequantisers: 256 threads turn raw stage r into dequantised tile d.
+        // Chunk id = i * 256 + tid covers (row, 16-byte chunk c); the swizzled
+        // destination is row * 128 + ((c ^ (row & 7)) << 4).
         const int tid = threadIdx.x - DEQ_WARP0 * 32;
-        int s = 0;
-        uint32_t ph = 0;
+        int r = 0, d = 0;
+        uint32_t rph = 0, dph = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
             for (int kb = 0; kb < g.k_blocks; ++kb) {
-                if (!mbar_wait(full_bar(s), ph, g.err, ERR_WAIT_DEQUANT)) { ok = false; break; }
-                const uint8_t *code = pCode(s);
-                uint8_t *dst = pD(s);
+                if (!mbar_wait_warp(raw_full(r), rph, g.err, ERR_WAIT_DEQUANT) ||
+                    !mbar_wait_warp(deq_empty(d), dph ^ 1, g.err, ERR_WAIT_DEQUANT)) { ok = false; break; }
+                const uint8_t *code = pCode(r);
+                uint8_t *dst = pD(d);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int id = i * DEQ_THREADS + tid;
                     const int row = id >> 3, c = id & 7;
                     uint4 out;
                     if (MODE == MODE_F16) {
-                        const uint16_t sh = pScale(s)[row * 2 + (c >> 2)];
+                        const uint16_t sh = pScale(r)[row * 2 + (c >> 2)];
                         const uint32_t s2 = static_cast<uint32_t>(sh) | (static_cast<uint32_t>(sh) << 16);
                         if (WBITS == 4) {
                             const uint32_t u = *reinterpret_cast<const uint32_t *>(code + row * 32 + c * 4);
@@ -347,11 +364,11 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tmA, const Args g) {
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(deq_bar(s));
-                if (++s == STAGES) { s = 0; ph ^= 1; }
+                if (lane == 0) mbar_arrive(deq_full(d));
+                if (++r == RS) { r = 0; rph ^= 1; }
+                if (++d == DS) { d = 0; dph ^= 1; }
             }
         }
-        (void)KB64_PER_STEP;
     }
 
     tc_fence_before();
@@ -404,22 +421,25 @@ int launch(const rkb_wgemm_desc *d, int *err, cudaStream_t stream) {
     return 0;
 }
 
+
 }  // namespace wq
 }  // namespace rkb
 
 extern "C" int rkb_wgemm_run(const rkb_wgemm_desc *d, int *err, cudaStream_t stream) {
     using namespace rkb::wq;
     if (d->M <= 0 || d->N <= 0 || d->K <= 0 || (d->N & 7) || (d->ldc & 7)) return ROCKET_E_SHAPE;
+#define RKB_WQ(MODE, BITS, OUT) return launch<MODE, BITS, OUT>(d, err, stream)
     if (d->a_f16) {
         if (d->w_bits == 4) {
-            if (d->out_kind == RKB_OUT_F32) return launch<MODE_F16, 4, RKB_OUT_F32>(d, err, stream);
-            if (d->out_kind == RKB_OUT_F16) return launch<MODE_F16, 4, RKB_OUT_F16>(d, err, stream);
+            if (d->out_kind == RKB_OUT_F32) { RKB_WQ(MODE_F16, 4, RKB_OUT_F32); }
+            if (d->out_kind == RKB_OUT_F16) { RKB_WQ(MODE_F16, 4, RKB_OUT_F16); }
         } else if (d->w_bits == 8) {
-            if (d->out_kind == RKB_OUT_F32) return launch<MODE_F16, 8, RKB_OUT_F32>(d, err, stream);
-            if (d->out_kind == RKB_OUT_F16) return launch<MODE_F16, 8, RKB_OUT_F16>(d, err, stream);
+            if (d->out_kind == RKB_OUT_F32) { RKB_WQ(MODE_F16, 8, RKB_OUT_F32); }
+            if (d->out_kind == RKB_OUT_F16) { RKB_WQ(MODE_F16, 8, RKB_OUT_F16); }
         }
     } else if (d->w_bits == 4 && d->out_kind == RKB_OUT_I32) {
-        return launch<MODE_I8, 4, RKB_OUT_I32>(d, err, stream);
+        RKB_WQ(MODE_I8, 4, RKB_OUT_I32);
     }
+#undef RKB_WQ
     return ROCKET_E_UNSUPPORTED;
 }
