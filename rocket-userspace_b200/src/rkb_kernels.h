@@ -62,6 +62,9 @@ typedef struct {
 } rkb_wgemm_desc;
 
 int rkb_wgemm_run(const rkb_wgemm_desc *d, int *err_word, cudaStream_t stream);
+/* The a_f16 (group-wise) form with the dequantised weights fed from TMEM;
+ * rkb_wgemm_run routes a_f16 descriptors here. */
+int rkb_wgemm_ts_run(const rkb_wgemm_desc *d, int *err_word, cudaStream_t stream);
 
 /* Resident-weight packers (device -> device).  src is the row-major int8
  * weight [N, K] (values in [-8,7] when bits == 4); dst gets the tiled layout
