@@ -384,16 +384,33 @@ def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "
     stream = torch.cuda.ExternalStream(L.rocket_b200_stream(dev.fd))
 
     def timed(fn, n):
+        """Device time per call: device-resident operands enqueued back to back
+        (rocket_b200_set_async), CUDA events on the handle's stream."""
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        L.rocket_b200_set_async(1)
         a.record(stream)
         for _ in range(n):
             fn()
         b.record(stream)
+        rc = L.rocket_b200_sync(dev.fd)
+        L.rocket_b200_set_async(0)
+        assert rc == 0, rc
         torch.cuda.synchronize()
         return a.elapsed_time(b) / n
+
+    def kernel_ms(fn, n, family):
+        """Mean device duration of the library's kernels of `family` (CUDA events
+        around each launch on its own stream, rocket_b200_profile_*)."""
+        L.rocket_b200_profile_reset()
+        L.rocket_b200_profile_enable(1)
+        for _ in range(n):
+            fn()
+        L.rocket_b200_profile_enable(0)
+        cnt, tot = rkb.profile_snapshot().get(family, (0, 0.0))
+        return tot / max(cnt, 1)
 
     # config 2: fp16 512x4096x4096
     if "c2" in which:
@@ -401,10 +418,20 @@ def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "
         A = (torch.randn((M, K), device="cuda") / K ** 0.5).half()
         B = (torch.randn((N, K), device="cuda") / K ** 0.5).half()
         C = torch.empty((M, N), dtype=torch.float16, device="cuda")
-        ms = timed(lambda: dev.matmul_fp16(M, K, N, A, B, C), 50)
+        ms = timed(lambda: dev.matmul_fp16(M, K, N, A, B, C), 200)
         ref = torch.matmul(A, B.t())
-        t = timed(lambda: torch.matmul(A, B.t()), 50)
+        for _ in range(3):
+            torch.matmul(A, B.t())
+        ta, tb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ta.record()
+        for _ in range(200):
+            torch.matmul(A, B.t())
+        tb.record()
+        torch.cuda.synchronize()
+        t = ta.elapsed_time(tb) / 200
+        kms = kernel_ms(lambda: dev.matmul_fp16(M, K, N, A, B, C), 50, "gemm_f16_tcgen05")
         out["config2_fp16"] = {"tflops": 2 * M * N * K / ms / 1e9, "ms": ms,
+                               "kernel_tflops": 2 * M * N * K / kms / 1e9, "kernel_ms": kms,
                                "frac_of_measured_bf16": 2 * M * N * K / ms / 1e9 / peaks["bf16_tflops"],
                                "torch_cublas_tflops": 2 * M * N * K / t / 1e9,
                                "rel_fro_vs_cublas": float((C.float() - ref.float()).norm() / ref.float().norm())}

@@ -17,7 +17,7 @@ import os
 from ctypes import POINTER, c_char_p, c_float, c_int, c_int8, c_int32, c_long, c_size_t, c_uint64, c_void_p
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "librocketnpu.so")
+LIB_PATH = os.environ.get("ROCKET_LIB_PATH") or os.path.join(_HERE, "librocketnpu.so")
 
 ROCKET_OK = 0
 ROCKET_E_SHAPE = -1
@@ -154,7 +154,15 @@ def _load():
 
 lib = _load()
 
-from . import shard  # noqa: E402  (N-column sharding across ranks)
+def _load_shard():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(__name__ + ".shard", os.path.join(_HERE, "shard.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+shard = _load_shard()   # N-column sharding across ranks
 
 
 def declared_symbols() -> list[str]:

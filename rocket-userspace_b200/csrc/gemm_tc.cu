@@ -36,6 +36,7 @@ namespace dense {
 constexpr int BM = 128;            // UMMA M (cta_group::1)
 constexpr int BK_BYTES = 128;      // one 128-byte swizzle row per K-block
 constexpr int NUM_THREADS = 192;   // 6 warps
+constexpr int PREFETCH = 12;       // K-blocks of L2 prefetch ahead of the current load
 
 template <int BN>
 struct Cfg {
@@ -194,6 +195,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 const int mt = t % g.m_tiles, nt = t / g.m_tiles;
                 for (int kb = 0; kb < g.k_blocks; ++kb) {
+                    if (kb + PREFETCH < g.k_blocks) {   // L2 prefetch beyond the ring
+                        tma_prefetch_2d(&tmA, (kb + PREFETCH) * BK_ELEMS, mt * BM);
+                        tma_prefetch_2d(&tmB, (kb + PREFETCH) * BK_ELEMS, nt * BN);
+                    }
                     if (!mbar_wait(empty_bar(s), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) { ok = false; break; }
                     mbar_arrive_expect_tx(full_bar(s), C::STAGE_BYTES);
                     tma_load_2d(sA(s), &tmA, kb * BK_ELEMS, mt * BM, full_bar(s));
@@ -395,6 +400,10 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
             for (int t = cluster_id; t < num_tiles && ok; t += nclusters) {
                 const int mt = t % g.m_tiles, nt = t / g.m_tiles;
                 for (int kb = 0; kb < g.k_blocks; ++kb) {
+                    if (kb + PREFETCH < g.k_blocks) {
+                        tma_prefetch_2d(&tmA, (kb + PREFETCH) * BK_ELEMS, mt * 2 * BM + rank * BM);
+                        tma_prefetch_2d(&tmB, (kb + PREFETCH) * BK_ELEMS, nt * BN + rank * C::BNH);
+                    }
                     if (!mbar_wait(empty_bar(s), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) { ok = false; break; }
                     const uint32_t lf = mapa_shared(full_bar(s), 0);
                     if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * C::STAGE_BYTES);
@@ -521,7 +530,8 @@ int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
 // (single-CTA tiles 128 x BN, CTA-pair tiles 256 x BN on two SMs).  Returns
 // 0x100 | BN for the pair kernel, BN for the single-CTA one.
 inline int pick_variant(int M, int N) {
-    if (const char *e = getenv("ROCKET_GEMM_VARIANT")) {
+    static const char *e = getenv("ROCKET_GEMM_VARIANT");
+    if (e) {
         int v = atoi(e);
         if (v == 128 || v == 256 || v == 0x180 || v == 0x200 || v == 384 || v == 512) return v == 384 ? 0x180 : v == 512 ? 0x200 : v;
     }

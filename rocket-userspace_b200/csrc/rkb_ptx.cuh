@@ -115,6 +115,12 @@ RKB_DEV void tma_load_2d(uint32_t dst, const CUtensorMap *tm, int c0, int c1, ui
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(bar)
         : "memory");
 }
+// Pull a 2D tile into L2 ahead of its shared-memory load (no completion
+// tracking, no shared memory used).
+RKB_DEV void tma_prefetch_2d(const CUtensorMap *tm, int c0, int c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+                 ::"l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1) : "memory");
+}
 // Contiguous bulk copy global -> shared (no tensor map).  dst, src 16-byte
 // aligned and bytes a multiple of 16.
 RKB_DEV void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {

@@ -23,13 +23,26 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
     return fn;
 }
 
+// Per-thread cache of encoded tensor maps: encoding costs about a microsecond of
+// host time, which matters for short GEMMs issued back to back on the same
+// buffers.  Keyed on every argument of the encode.
+struct TmapKey {
+    const void *base;
+    long cols, rows, ld;
+    int dt, esize, box_cols, box_rows, swz;
+    bool operator==(const TmapKey &o) const {
+        return base == o.base && cols == o.cols && rows == o.rows && ld == o.ld && dt == o.dt &&
+               esize == o.esize && box_cols == o.box_cols && box_rows == o.box_rows && swz == o.swz;
+    }
+};
+
 // Row-major 2D tensor [rows, cols] (cols contiguous, ld elements between rows),
 // box = box_cols x box_rows, 128-byte swizzle, zero fill outside the tensor.
 // Returns 0 on success.  box_cols * esize must be <= 128 for the swizzle and
 // the base / row pitch must be 16-byte aligned.
-inline int make_tmap_2d(CUtensorMap *tm, const void *base, CUtensorMapDataType dt, int esize,
-                        long cols, long rows, long ld, int box_cols, int box_rows,
-                        CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+inline int encode_tmap_2d(CUtensorMap *tm, const void *base, CUtensorMapDataType dt, int esize,
+                          long cols, long rows, long ld, int box_cols, int box_rows,
+                          CUtensorMapSwizzle swz) {
     auto enc = tmap_encoder();
     if (!enc) {
         fprintf(stderr, "rkb: cuTensorMapEncodeTiled unavailable\n");
@@ -49,6 +62,29 @@ inline int make_tmap_2d(CUtensorMap *tm, const void *base, CUtensorMapDataType d
         return -1;
     }
     return 0;
+}
+
+inline int make_tmap_2d(CUtensorMap *tm, const void *base, CUtensorMapDataType dt, int esize,
+                        long cols, long rows, long ld, int box_cols, int box_rows,
+                        CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+    constexpr int SLOTS = 64;
+    static thread_local TmapKey keys[SLOTS];
+    static thread_local CUtensorMap maps[SLOTS];
+    static thread_local bool valid[SLOTS];
+    const TmapKey k{base, cols, rows, ld, static_cast<int>(dt), esize, box_cols, box_rows, static_cast<int>(swz)};
+    const size_t h = (reinterpret_cast<uintptr_t>(base) >> 8) ^ static_cast<size_t>(cols * 31 + rows * 17 + box_rows);
+    const int slot = static_cast<int>(h % SLOTS);
+    if (valid[slot] && keys[slot] == k) {
+        *tm = maps[slot];
+        return 0;
+    }
+    int rc = encode_tmap_2d(tm, base, dt, esize, cols, rows, ld, box_cols, box_rows, swz);
+    if (rc == 0) {
+        keys[slot] = k;
+        maps[slot] = *tm;
+        valid[slot] = true;
+    }
+    return rc;
 }
 
 }  // namespace rkb

@@ -430,7 +430,8 @@ extern "C" int rkb_wgemm_run(const rkb_wgemm_desc *d, int *err, cudaStream_t str
     if (d->M <= 0 || d->N <= 0 || d->K <= 0 || (d->N & 7) || (d->ldc & 7)) return ROCKET_E_SHAPE;
 #define RKB_WQ(MODE, BITS, OUT) return launch<MODE, BITS, OUT>(d, err, stream)
     if (d->a_f16) {
-        if (getenv("ROCKET_WGEMM_SMEM_B") == nullptr) return rkb_wgemm_ts_run(d, err, stream);
+        static const bool smem_b = getenv("ROCKET_WGEMM_SMEM_B") != nullptr;
+        if (!smem_b) return rkb_wgemm_ts_run(d, err, stream);
         if (d->w_bits == 4) {
             if (d->out_kind == RKB_OUT_F32) { RKB_WQ(MODE_F16, 4, RKB_OUT_F32); }
             if (d->out_kind == RKB_OUT_F16) { RKB_WQ(MODE_F16, 4, RKB_OUT_F16); }
