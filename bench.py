@@ -404,11 +404,18 @@ def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "
     def kernel_ms(fn, n, family):
         """Mean device duration of the library's kernels of `family` (CUDA events
         around each launch on its own stream, rocket_b200_profile_*)."""
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
         L.rocket_b200_profile_reset()
         L.rocket_b200_profile_enable(1)
+        L.rocket_b200_set_async(1)   # back to back: events bracket device work only
         for _ in range(n):
             fn()
+        rc = L.rocket_b200_sync(dev.fd)
+        L.rocket_b200_set_async(0)
         L.rocket_b200_profile_enable(0)
+        assert rc == 0, rc
         cnt, tot = rkb.profile_snapshot().get(family, (0, 0.0))
         return tot / max(cnt, 1)
 

@@ -60,6 +60,8 @@ struct Args {
     const __half *residual;
     long ldr;
     int act;
+    int k_splits, kb_per_split;   // split-K: unit t -> (split, tile); partials at C + split*split_stride
+    long split_stride;
     int *err;
 };
 
@@ -302,6 +304,7 @@ int launch(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
     g.bias = static_cast<const __half *>(d->bias);
     g.residual = static_cast<const __half *>(d->residual);
     g.ldr = d->ldr; g.act = d->act;
+    g.k_splits = 1; g.kb_per_split = g.k_blocks; g.split_stride = 0;
     g.err = err;
     const int tiles = g.m_tiles * g.n_tiles;
     const int sms = rkb_device_sm_count(dev);
@@ -388,9 +391,15 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int num_tiles = g.m_tiles * g.n_tiles;
+    const int mn_tiles = g.m_tiles * g.n_tiles;
+    const int num_tiles = mn_tiles * g.k_splits;
     const int cluster_id = blockIdx.x >> 1;
     const int nclusters = gridDim.x >> 1;
+    auto kb_lo = [&](int t) { return (t / mn_tiles) * g.kb_per_split; };
+    auto kb_hi = [&](int t) {
+        const int e = (t / mn_tiles + 1) * g.kb_per_split;
+        return e < g.k_blocks ? e : g.k_blocks;
+    };
 
     if (warp == 0) {
         if (lane == 0) {
@@ -398,9 +407,11 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
             uint32_t ph = 0;
             bool ok = true;
             for (int t = cluster_id; t < num_tiles && ok; t += nclusters) {
-                const int mt = t % g.m_tiles, nt = t / g.m_tiles;
-                for (int kb = 0; kb < g.k_blocks; ++kb) {
-                    if (kb + PREFETCH < g.k_blocks) {
+                const int tt = t % mn_tiles;
+                const int mt = tt % g.m_tiles, nt = tt / g.m_tiles;
+                const int kb1 = kb_hi(t);
+                for (int kb = kb_lo(t); kb < kb1; ++kb) {
+                    if (kb + PREFETCH < kb1) {
                         tma_prefetch_2d(&tmA, (kb + PREFETCH) * BK_ELEMS, mt * 2 * BM + rank * BM);
                         tma_prefetch_2d(&tmB, (kb + PREFETCH) * BK_ELEMS, nt * BN + rank * C::BNH);
                     }
@@ -425,7 +436,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
                 if (!mbar_wait(tempty_bar(b), aph ^ 1, g.err, ERR_WAIT_MMA_ACC)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t dcol = tmem_base + b * BN;
-                for (int kb = 0; kb < g.k_blocks; ++kb) {
+                const int kb0 = kb_lo(t), kb1 = kb_hi(t);
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(full_bar(s), ph, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t adesc = smem_desc_sw128(sA(s));
@@ -433,7 +445,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
                         const uint64_t koff = static_cast<uint64_t>((k * 32) >> 4);
-                        const uint32_t acc = (kb | k) != 0;
+                        const uint32_t acc = (kb != kb0) || (k != 0);
                         if (KIND == RKB_IN_F16) tc_mma_f16_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
                         else                    tc_mma_i8_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
                     }
@@ -461,16 +473,20 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
             const uint32_t aph = (it >> 1) & 1;
             if (!mbar_wait(tfull_bar(b), aph, g.err, ERR_WAIT_EPILOGUE)) break;
             tc_fence_after();
-            const int mt = t % g.m_tiles, nt = t / g.m_tiles;
+            const int tt = t % mn_tiles;
+            const int mt = tt % g.m_tiles, nt = tt / g.m_tiles;
             const int row = mt * 2 * BM + rank * BM + q * 32 + lane;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
+            Args gs = g;   // split-K partial slab of this unit
+            if (g.k_splits > 1)
+                gs.C = static_cast<float *>(g.C) + static_cast<long>(t / mn_tiles) * g.split_stride;
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 uint32_t r[32];
                 tmem_ld32(tbase + c, r);
                 tmem_ld_wait();
                 const int col = nt * BN + c;
-                if (col < g.N) store_chunk<OUT>(g, row, col, r);
+                if (col < g.N) store_chunk<OUT>(gs, row, col, r);
             }
             tc_fence_before();
             __syncwarp();
@@ -487,7 +503,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
 }
 
 template <int KIND, int OUT, int BN>
-int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
+int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream, int splits = 1) {
     using C = Cfg2<BN>;
     static std::once_flag attr_once[16];
     int dev = 0;
@@ -513,8 +529,18 @@ int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
     g.bias = static_cast<const __half *>(d->bias);
     g.residual = static_cast<const __half *>(d->residual);
     g.ldr = d->ldr; g.act = d->act;
+    g.k_splits = splits;
+    g.kb_per_split = (g.k_blocks + splits - 1) / splits;
+    g.split_stride = static_cast<long>(d->M) * d->N;
+    if (splits > 1) {   // fp32 partial slabs [splits][M][N], no epilogue extras
+        g.C = d->workspace;
+        g.ldc = d->N;
+        g.row_scale = g.col_scale = nullptr;
+        g.bias = g.residual = nullptr;
+        g.act = RKB_ACT_NONE;
+    }
     g.err = err;
-    const int tiles = g.m_tiles * g.n_tiles;
+    const int tiles = g.m_tiles * g.n_tiles * splits;
     const int pairs = rkb_device_sm_count(dev) / 2;
     const int grid = 2 * (tiles < pairs ? tiles : pairs);
     gemm2_kernel<KIND, OUT, BN><<<grid, NUM_THREADS, C::SMEM, stream>>>(ta, tb, g);
@@ -551,13 +577,93 @@ inline int pick_variant(int M, int N) {
     return code;
 }
 
+// Split-K reduction: C = epilogue(sum over splits of the fp32 partials), the
+// splits summed in index order (deterministic).  8 outputs per thread.
+template <int OUT>
+__global__ void split_reduce(const float *__restrict__ ws, int splits, long stride, int M, int N,
+                             void *C, long ldc, const __half *bias, int act, const __half *res, long ldr) {
+    const long n8 = static_cast<long>(M) * (N / 8);
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n8;
+         i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const int row = static_cast<int>(i / (N / 8)), col = static_cast<int>(i % (N / 8)) * 8;
+        float f[8];
+        const float4 *p0 = reinterpret_cast<const float4 *>(ws + static_cast<long>(row) * N + col);
+        float4 a = p0[0], b = p0[1];
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+        for (int s = 1; s < splits; ++s) {
+            const float4 *p = reinterpret_cast<const float4 *>(ws + s * stride + static_cast<long>(row) * N + col);
+            a = p[0]; b = p[1];
+            f[0] += a.x; f[1] += a.y; f[2] += a.z; f[3] += a.w; f[4] += b.x; f[5] += b.y; f[6] += b.z; f[7] += b.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (bias) f[j] += __half2float(bias[col + j]);
+            f[j] = apply_act(f[j], act);
+            if (res) f[j] += __half2float(res[static_cast<long>(row) * ldr + col + j]);
+        }
+        if (OUT == RKB_OUT_F32) {
+            float4 *o = reinterpret_cast<float4 *>(static_cast<float *>(C) + static_cast<long>(row) * ldc + col);
+            o[0] = make_float4(f[0], f[1], f[2], f[3]);
+            o[1] = make_float4(f[4], f[5], f[6], f[7]);
+        } else {
+            uint32_t h[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                __half2 p = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+                h[j] = *reinterpret_cast<uint32_t *>(&p);
+            }
+            *reinterpret_cast<uint4 *>(static_cast<__half *>(C) + static_cast<long>(row) * ldc + col) =
+                make_uint4(h[0], h[1], h[2], h[3]);
+        }
+    }
+}
+
+// Split count for fp16 inputs (ROCKET_GEMM_SPLITK = 2..4; default 1 = off):
+// split-K on the CTA-pair 256x256 kernel.  Opt-in because at the one shape
+// class it targets (small M, e.g. 512 x 4096 x 4096) it measured no faster
+// than the unsplit kernels; it is kept, tested, for shapes where it may be.
+inline int pick_splits(const rkb_gemm_desc *d) {
+    if (d->in_kind != RKB_IN_F16 || d->row_scale || d->col_scale) return 1;
+    const char *e = getenv("ROCKET_GEMM_SPLITK");
+    if (!e) return 1;
+    int s = atoi(e);
+    const int kblocks = (d->K * 2 + BK_BYTES - 1) / BK_BYTES;
+    if (s > 4) s = 4;
+    while (s > 1 && kblocks / s < 4) --s;
+    return s < 1 ? 1 : s;
+}
+
 }  // namespace dense
 }  // namespace rkb
+
+extern "C" size_t rkb_gemm_workspace_bytes(const rkb_gemm_desc *d) {
+    const int s = rkb::dense::pick_splits(d);
+    return s > 1 ? static_cast<size_t>(s) * d->M * d->N * sizeof(float) : 0;
+}
 
 extern "C" int rkb_gemm_run(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
     using namespace rkb::dense;
     if (d->M <= 0 || d->N <= 0 || d->K <= 0) return ROCKET_E_SHAPE;
     if ((d->N & 7) || (d->ldc & 7)) return ROCKET_E_SHAPE;
+    const int splits = pick_splits(d);
+    if (splits > 1) {
+        if (!d->workspace || (d->N & 7)) return ROCKET_E_NOMEM;
+        int rc = launch2<RKB_IN_F16, RKB_OUT_F32, 256>(d, err, stream, splits);
+        if (rc) return rc;
+        const long n8 = static_cast<long>(d->M) * (d->N / 8);
+        int grid = static_cast<int>((n8 + 255) / 256);
+        if (grid > 148 * 8) grid = 148 * 8;
+        const long stride = static_cast<long>(d->M) * d->N;
+        const __half *bias = static_cast<const __half *>(d->bias);
+        const __half *res = static_cast<const __half *>(d->residual);
+        if (d->out_kind == RKB_OUT_F16)
+            split_reduce<RKB_OUT_F16><<<grid, 256, 0, stream>>>(static_cast<const float *>(d->workspace), splits,
+                                                                 stride, d->M, d->N, d->C, d->ldc, bias, d->act, res, d->ldr);
+        else
+            split_reduce<RKB_OUT_F32><<<grid, 256, 0, stream>>>(static_cast<const float *>(d->workspace), splits,
+                                                                 stride, d->M, d->N, d->C, d->ldc, bias, d->act, res, d->ldr);
+        return cudaGetLastError() == cudaSuccess ? 0 : ROCKET_E_DEVICE;
+    }
     const int v = pick_variant(d->M, d->N);
 #define RKB_DISPATCH(KIND, OUT)                                                   \
     switch (v) {                                                                  \

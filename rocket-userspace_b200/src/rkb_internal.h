@@ -21,7 +21,7 @@
 
 enum rkb_scratch_slot {
     RKB_SCR_A = 0, RKB_SCR_B, RKB_SCR_C, RKB_SCR_AS, RKB_SCR_BS, RKB_SCR_AUX,
-    RKB_SCR_ROW, RKB_SCR_WQ, RKB_SCR_WS, RKB_NSCR
+    RKB_SCR_ROW, RKB_SCR_WQ, RKB_SCR_WS, RKB_SCR_SPLIT, RKB_NSCR
 };
 
 /* Kernel families timed by the profiler (rocket_b200_profile_*). */

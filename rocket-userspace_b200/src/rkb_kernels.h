@@ -37,7 +37,13 @@ typedef struct {
     int act;                   /* RKB_ACT_* */
     const void *residual;      /* fp16, or NULL */
     long ldr;
+    /* split-K workspace (fp32), sized by rkb_gemm_workspace_bytes; may be NULL
+     * when that returns 0 */
+    void *workspace;
 } rkb_gemm_desc;
+
+/* Device workspace rkb_gemm_run will use for this descriptor (0 = none). */
+size_t rkb_gemm_workspace_bytes(const rkb_gemm_desc *d);
 
 enum rkb_act { RKB_ACT_NONE = 0, RKB_ACT_GELU = 1, RKB_ACT_SILU = 2 };
 

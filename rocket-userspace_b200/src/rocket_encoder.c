@@ -133,7 +133,9 @@ static void enc_gemm(enc_call *c, int M, int N, int K, const void *A, long lda, 
     d.M = M; d.N = N; d.K = K;
     d.A = A; d.lda = lda; d.B = W; d.ldb = K; d.C = C; d.ldc = ldc;
     d.bias = bias; d.act = act; d.residual = res; d.ldr = ldr;
-    rkb_count(0, 1);
+    const size_t wb = rkb_gemm_workspace_bytes(&d);
+    if (wb && !(d.workspace = enc_tmp(c, wb))) return;
+    rkb_count(0, wb ? 2 : 1);
     int ps = rkb_prof_begin(c->h);
     enc_check(c, rkb_gemm_run(&d, c->h->err_dev, c->h->stream));
     rkb_prof_end(c->h, ps, RKB_K_GEMM_F16);

@@ -202,3 +202,23 @@ def test_groupwise_config3_rows_sampled(rkb, dev, orc):
     C = dC.cpu().numpy()
     rows = [0, 127, 128, 1000, 2047]
     close_enough(orc, C[rows], orc.gw_ref(A[rows], B, a[rows], b, group, nthreads=8))
+
+
+@pytest.mark.parametrize("M,K,N", [(512, 4096, 4096), (260, 8192, 1024), (64, 4096, 2048)])
+def test_fp16_small_m_split_k(dev, orc, M, K, N, monkeypatch):
+    """The opt-in split-K CTA-pair path (fp32 partials reduced in a fixed order):
+    results stay within the fp16 bound and are deterministic."""
+    import torch
+    monkeypatch.setenv("ROCKET_GEMM_SPLITK", "3")
+    A = orc.normal_f16(M + 3, 1.0 / np.sqrt(K), (M, K))
+    B = orc.normal_f16(N + 4, 1.0, (N, K))
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    C1 = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    C2 = torch.empty_like(C1)
+    assert dev.matmul_fp16(M, K, N, dA, dB, C1) == 0
+    assert dev.matmul_fp16(M, K, N, dA, dB, C2) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(C1, C2)
+    rows = list(range(0, M, max(1, M // 16))) + [M - 1]
+    R, _ = orc.matmul_fp16(A[rows], B, nthreads=8)
+    close_enough(orc, C1.cpu().numpy()[rows].astype(np.float32), R)
