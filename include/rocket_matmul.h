@@ -92,6 +92,46 @@ int rocket_matmul_int4_groupwise(int fd, int M, int K, int N,
                                  const float *a_scale, const float *b_scale,
                                  float *Cf, int group);
 
+/* fp16 x fp16 -> fp32 output (fp32 accumulate, no fp16 narrowing).
+ * Replaces src/rocket_matmul.c:3620. */
+int rocket_matmul_fp16_f32out(int fd, int M, int K, int N,
+                              const _Float16 *A, const _Float16 *B, float *C);
+
+/* nbatch independent same-shape fp16 matmuls C[i] = A[i] B[i]^T queued on one
+ * stream with one completion wait.  Replaces src/rocket_matmul.c:2042-2330. */
+int rocket_matmul_fp16_batch(int fd, int M, int K, int N, int nbatch,
+                             const _Float16 *const *A, const _Float16 *const *B,
+                             _Float16 *const *C);
+typedef struct rocket_mm_batch rocket_mm_batch;
+rocket_mm_batch *rocket_mm_batch_create(int fd);
+void             rocket_mm_batch_free(rocket_mm_batch *b);
+int rocket_mm_batch_run(rocket_mm_batch *b, int M, int K, int N, int nbatch,
+                        const _Float16 *const *A, const _Float16 *const *B,
+                        _Float16 *const *C);
+
+/* int16 / bf16 geometry preview (K%32, N%16, M%4 or M==1). */
+int rocket_matmul_plan_int16(int M, int K, int N, int *Mt, int *Kt, int *Nt);
+/* Exact int16 x int16 -> int64 via four int8 GEMMs on signed hi/lo bytes;
+ * inputs clamped to [-32768, 32639].  K%32, N%32.  Replaces src/rocket_matmul.c:3377. */
+int rocket_matmul_int16_exact(int fd, int M, int K, int N,
+                              const int16_t *A, const int16_t *B, int64_t *C);
+
+/* bf16: fp32 A/B truncated to bf16, fp32 accumulate and output.
+ * Replaces src/rocket_matmul.c:3454 and src/rocket_bf16_stream.c. */
+int rocket_matmul_plan_bf16(int M, int K, int N, int *Mt, int *Kt, int *Nt);
+int rocket_matmul_bf16(int fd, int M, int K, int N, const float *A, const float *B, float *C);
+int rocket_matmul_bf16_mt(int M, int K, int N, const float *A, const float *B, float *C, int nthreads);
+typedef struct rocket_bf16_stream rocket_bf16_stream;
+rocket_bf16_stream *rocket_bf16_stream_create(int nthreads);
+void                rocket_bf16_stream_free(rocket_bf16_stream *s);
+int rocket_matmul_bf16_stream(rocket_bf16_stream *s, int M, int K, int N,
+                              const float *A, const float *B, float *C);
+
+/* tf32: fp32 A/B fed to the tf32 tensor-core path, fp32 accumulate and output.
+ * K%16, N%16.  Replaces src/rocket_matmul.c:3840. */
+int rocket_matmul_plan_tf32(int M, int K, int N, int *Mt, int *Kt, int *Nt);
+int rocket_matmul_tf32(int fd, int M, int K, int N, const float *A, const float *B, float *C);
+
 /* ---- multi-GPU fan-out ---------------------------------------------------
  * Split N across `nthreads` GPUs (clamped to [1, 8] and to the visible device
  * count; nthreads > devices wraps round-robin), one host worker thread per
@@ -116,6 +156,21 @@ rocket_weights *rocket_weights_pack(rocket_ctx *ctx, int M, int K, int N, const 
 void            rocket_weights_free(rocket_ctx *ctx, rocket_weights *w);
 int rocket_matmul_fp16_prepacked(rocket_ctx *ctx, int M, int K, int N,
                                  const _Float16 *A, _Float16 *C, rocket_weights *w);
+
+/* ---- streaming fp16: weights re-uploaded every call ------------------------
+ * A stream keeps its workers (GPUs) and weight buffers across calls; each call
+ * uploads this call's B (or, fused, the N-concatenation of nseg weights that
+ * share A -- QKV, gate+up) and runs the N-split matmul.  C of the fused form is
+ * [M, sum Ns].  Not thread-safe per stream.  Replaces src/rocket_prepacked.c:459-505. */
+#define ROCKET_MAX_FUSE 8
+typedef struct rocket_stream rocket_stream;
+rocket_stream *rocket_stream_create(int nthreads);
+void           rocket_stream_free(rocket_stream *s);
+int rocket_matmul_fp16_stream(rocket_stream *s, int M, int K, int N,
+                              const _Float16 *A, const _Float16 *B, _Float16 *C);
+int rocket_matmul_fp16_stream_fused(rocket_stream *s, int M, int K,
+                                    const _Float16 *const *Bs, const int *Ns, int nseg,
+                                    const _Float16 *A, _Float16 *C);
 
 /* ---- resident int8 (W8A8) --------------------------------------------------
  * Per-channel form returns raw int32, group-wise form the fp32 scaled sum.

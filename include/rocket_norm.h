@@ -13,6 +13,8 @@ typedef ROCKET_FLOAT16_T _Float16;
 #ifdef __cplusplus
 extern "C" {
 #endif
+/* out[m, n] = in[m, n] * r[m] (r fp32 [M]).  Replaces src/rocket_norm.c:21-60. */
+int rocket_scale_rows_fp16(int fd, int M, int N, const _Float16 *in, const float *r, _Float16 *out);
 /* out = x / sqrt(mean(x^2) + eps) * weight.  Replaces src/rocket_norm.c:72-126. */
 int rocket_rmsnorm_fp16(int fd, int M, int H, const _Float16 *x, const _Float16 *weight,
                         float eps, _Float16 *out);

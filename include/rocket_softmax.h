@@ -13,6 +13,10 @@ extern "C" {
 #endif
 int rocket_softmax_fp16(int fd, int M, int N, const _Float16 *in, _Float16 *out);
 int rocket_logsoftmax_fp16(int fd, int M, int N, const _Float16 *in, _Float16 *out);
+/* loss[m] = logsumexp(logits[m, :]) - logits[m, target[m]] (fp32 [M]); a target
+ * outside [0, N) contributes 0 for the logit term, as in src/rocket_softmax.c:141-155. */
+int rocket_cross_entropy_fp16(int fd, int M, int N, const _Float16 *logits, const int *target,
+                              float *loss);
 #ifdef __cplusplus
 }
 #endif

@@ -248,3 +248,82 @@ def encoder_golden_inputs():
 
 ACT_KINDS = [0, 1, 2, 3, 4, 5, 7, 8, 9, 10, 11, 12, 13, 14, 15, 18]
 POSITIVE_KINDS = (7, 8, 9, 18)
+
+
+# ---- reductions (oracle.c, bit-exact restatements of the reference's host refs) ----
+def _sig_red():
+    P, I = ctypes.c_void_p, ctypes.c_int
+    for n, a in {"orc_reduce_feature_f16": [I, I, P, I, P], "orc_cumsum_f16": [I, I, P, I, I, P],
+                 "orc_scale_rows_f16": [I, I, P, P, P], "orc_cross_entropy_f16": [I, I, P, P, P]}.items():
+        getattr(lib, n).restype = None
+        getattr(lib, n).argtypes = a
+
+
+_sig_red()
+
+
+def reduce_feature(x, mean=False):
+    M, H = x.shape
+    out = np.empty(M, np.float32)
+    lib.orc_reduce_feature_f16(M, H, _h(x), int(mean), out.ctypes.data)
+    return out
+
+
+def cumsum(x, exclusive=False, reverse=False):
+    M, N = x.shape
+    y = np.empty((M, N), np.float16)
+    lib.orc_cumsum_f16(M, N, _h(x), int(exclusive), int(reverse), y.ctypes.data)
+    return y
+
+
+def scale_rows(x, r):
+    M, N = x.shape
+    y = np.empty((M, N), np.float16)
+    lib.orc_scale_rows_f16(M, N, _h(x), np.ascontiguousarray(r, np.float32).ctypes.data, y.ctypes.data)
+    return y
+
+
+def cross_entropy(x, target):
+    M, N = x.shape
+    loss = np.empty(M, np.float32)
+    lib.orc_cross_entropy_f16(M, N, _h(x), np.ascontiguousarray(target, np.int32).ctypes.data,
+                              loss.ctypes.data)
+    return loss
+
+
+# ---- dtype matmuls (C = A . B^T, fp64 references) ----
+def bf16_trunc(a):
+    """fp32 -> bf16 -> fp32 by dropping the low 16 bits (src/rocket_matmul.c:3456-3458)."""
+    return (np.ascontiguousarray(a, np.float32).view(np.uint32) & np.uint32(0xFFFF0000)).view(np.float32)
+
+
+def matmul_bf16(A, B):
+    """Truncated-bf16 products accumulated in fp64 (tests/matmul_bf16_tiled_rocket.c ref)."""
+    return bf16_trunc(A).astype(np.float64) @ bf16_trunc(B).astype(np.float64).T
+
+
+def matmul_f64(A, B):
+    """fp64 product of the raw inputs (the tf32 and fp16->fp32 gates' reference)."""
+    return np.asarray(A, np.float64) @ np.asarray(B, np.float64).T
+
+
+def int16_clamp(a):
+    """The exact int16 route's input domain [-32768, 32639] (src/rocket_matmul.c:3397-3403)."""
+    return np.clip(np.asarray(a, np.int64), -32768, 32639)
+
+
+def matmul_int16_exact(A, B):
+    """int64 A . B^T over the clamped inputs (bit-exact target)."""
+    return int16_clamp(A) @ int16_clamp(B).T
+
+
+def reduce_golden_inputs():
+    """Seeded inputs of tests/golden/reduce_golden.npz: x [37, 300] fp16 ~ N(0, 1)
+    (ragged: neither dimension a multiple of 32), per-row scales r [37], logits
+    [33, 1000] ~ N(0, 3) with targets that include -1 and N (out of range)."""
+    x = normal_f16(71, 1.0, (37, 300))
+    r = uniform_f32(72, -2.0, 2.0, (37,))
+    logits = normal_f16(73, 3.0, (33, 1000))
+    t = (np.arange(33, dtype=np.int64) * 397 % 1000).astype(np.int32)
+    t[5], t[11] = -1, 1000
+    return {"x": x, "r": r, "logits": logits, "target": t}

@@ -419,3 +419,53 @@ void orc_encoder_block_f16(int T, int d, int nh, int dff, const uint16_t *x,
     for (size_t i = 0; i < Td; i++) out[i] = dh16(hd(xa[i]) + f2[i] + (c2 ? hd(c2[i % d]) : 0.0));
     free(ln); free(attn); free(xa); free(lnd); free(f1); free(f2);
 }
+
+/* ---- reductions (each a double-accumulating row loop) ---- */
+
+/* src/rocket_reduce.c:380-390: out[m] = sum_h in[m, h] (x 1/H when mean) */
+void orc_reduce_feature_f16(int M, int H, const uint16_t *x, int mean, float *out)
+{
+    const double inv = mean ? 1.0 / (double)H : 1.0;
+    for (int m = 0; m < M; m++) {
+        double acc = 0;
+        for (int h = 0; h < H; h++) acc += hd(x[(size_t)m * H + h]);
+        out[m] = (float)(acc * inv);
+    }
+}
+
+/* src/rocket_reduce.c:445-462: inclusive / exclusive, forward / reverse prefix sums */
+void orc_cumsum_f16(int M, int N, const uint16_t *x, int exclusive, int reverse, uint16_t *y)
+{
+    for (int m = 0; m < M; m++) {
+        const uint16_t *r = x + (size_t)m * N;
+        uint16_t *o = y + (size_t)m * N;
+        double acc = 0;
+        for (int i = 0; i < N; i++) {
+            const int j = reverse ? N - 1 - i : i;
+            if (exclusive) { o[j] = dh16(acc); acc += hd(r[j]); }
+            else           { acc += hd(r[j]); o[j] = dh16(acc); }
+        }
+    }
+}
+
+/* src/rocket_norm.c:21-30: out[m, n] = (fp16)((float)in[m, n] * r[m]) in float */
+void orc_scale_rows_f16(int M, int N, const uint16_t *x, const float *r, uint16_t *y)
+{
+    for (int m = 0; m < M; m++)
+        for (int n = 0; n < N; n++)
+            y[(size_t)m * N + n] = dh16((double)(orc_h2f(x[(size_t)m * N + n]) * r[m]));
+}
+
+/* src/rocket_softmax.c:141-156: loss = logsumexp(row) - row[target]; out-of-range target -> 0 */
+void orc_cross_entropy_f16(int M, int N, const uint16_t *x, const int *target, float *loss)
+{
+    for (int m = 0; m < M; m++) {
+        const uint16_t *r = x + (size_t)m * N;
+        double mx = -INFINITY, s = 0;
+        for (int n = 0; n < N; n++) if (hd(r[n]) > mx) mx = hd(r[n]);
+        for (int n = 0; n < N; n++) s += exp(hd(r[n]) - mx);
+        const int t = target[m];
+        const double g = (t >= 0 && t < N) ? hd(r[t]) : 0.0;
+        loss[m] = (float)(mx + log(s) - g);
+    }
+}

@@ -56,6 +56,12 @@ void orc_encoder_block_f16(int T, int d, int nh, int dff, const uint16_t *x,
                            const uint16_t *W1, const uint16_t *c1, const uint16_t *W2,
                            const uint16_t *c2, float eps, uint16_t *out);
 
+/* reductions */
+void orc_reduce_feature_f16(int M, int H, const uint16_t *x, int mean, float *out);
+void orc_cumsum_f16(int M, int N, const uint16_t *x, int exclusive, int reverse, uint16_t *y);
+void orc_scale_rows_f16(int M, int N, const uint16_t *x, const float *r, uint16_t *y);
+void orc_cross_entropy_f16(int M, int N, const uint16_t *x, const int *target, float *loss);
+
 #ifdef __cplusplus
 }
 #endif

@@ -133,6 +133,32 @@ _SIGS += [
      [c_int, c_int, c_int, c_int, c_int, c_int] + [_P] * 17 + [_F, _P]),
 ]
 
+_SIGS += [
+    ("rocket_reduce_feature_fp16", c_int, [c_int, c_int, c_int, _P, _P, c_int]),
+    ("rocket_cumsum_fp16", c_int, [c_int, c_int, c_int, _P, _P, c_int, c_int]),
+    ("rocket_scale_rows_fp16", c_int, [c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_cross_entropy_fp16", c_int, [c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_fp16_f32out", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_fp16_batch", c_int, [c_int, c_int, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_mm_batch_create", _P, [c_int]),
+    ("rocket_mm_batch_free", None, [_P]),
+    ("rocket_mm_batch_run", c_int, [_P, c_int, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_plan_int16", c_int, [c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_int16_exact", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_plan_bf16", c_int, [c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_bf16", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_bf16_mt", c_int, [c_int, c_int, c_int, _P, _P, _P, c_int]),
+    ("rocket_bf16_stream_create", _P, [c_int]),
+    ("rocket_bf16_stream_free", None, [_P]),
+    ("rocket_matmul_bf16_stream", c_int, [_P, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_plan_tf32", c_int, [c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_tf32", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_stream_create", _P, [c_int]),
+    ("rocket_stream_free", None, [_P]),
+    ("rocket_matmul_fp16_stream", c_int, [_P, c_int, c_int, c_int, _P, _P, _P]),
+    ("rocket_matmul_fp16_stream_fused", c_int, [_P, c_int, c_int, _P, _P, c_int, _P, _P]),
+]
+
 ENCODER_KEYS = ["ln1_g", "ln1_b", "Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo", "ln2_g", "ln2_b",
                 "W1", "b1", "W2", "b2"]
 

@@ -33,6 +33,29 @@
 namespace rkb {
 namespace dense {
 
+// Per input kind: element size, instruction descriptor, TMA element type.
+template <int KIND> struct Kind;
+template <> struct Kind<RKB_IN_F16> {
+    static constexpr int ESIZE = 2;
+    static constexpr CUtensorMapDataType DT = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    static constexpr uint32_t idesc(int m, int n) { return idesc_f16_f32acc(m, n); }
+};
+template <> struct Kind<RKB_IN_BF16> {
+    static constexpr int ESIZE = 2;
+    static constexpr CUtensorMapDataType DT = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    static constexpr uint32_t idesc(int m, int n) { return idesc_f32acc_fmt(1, m, n); }
+};
+template <> struct Kind<RKB_IN_TF32> {
+    static constexpr int ESIZE = 4;
+    static constexpr CUtensorMapDataType DT = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    static constexpr uint32_t idesc(int m, int n) { return idesc_f32acc_fmt(2, m, n); }
+};
+template <> struct Kind<RKB_IN_I8> {
+    static constexpr int ESIZE = 1;
+    static constexpr CUtensorMapDataType DT = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    static constexpr uint32_t idesc(int m, int n) { return idesc_s8_s32acc(m, n); }
+};
+
 constexpr int BM = 128;            // UMMA M (cta_group::1)
 constexpr int BK_BYTES = 128;      // one 128-byte swizzle row per K-block
 constexpr int NUM_THREADS = 192;   // 6 warps
@@ -141,11 +164,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const Args g) {
     using C = Cfg<BN>;
     constexpr int STAGES = C::STAGES;
-    constexpr int BK_ELEMS = (KIND == RKB_IN_F16) ? 64 : 128;
-    constexpr int UMMA_K_BYTES = 32;                      // 16 fp16 or 32 int8 per MMA
+    constexpr int BK_ELEMS = BK_BYTES / Kind<KIND>::ESIZE;
+    constexpr int UMMA_K_BYTES = 32;                      // 16 fp16/bf16, 8 tf32 or 32 int8 per MMA
     constexpr int K_STEPS = BK_BYTES / UMMA_K_BYTES;      // 4 MMAs per K-block
-    constexpr uint32_t IDESC = (KIND == RKB_IN_F16) ? idesc_f16_f32acc(BM, BN)
-                                                    : idesc_s8_s32acc(BM, BN);
+    constexpr uint32_t IDESC = Kind<KIND>::idesc(BM, BN);
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -230,8 +252,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     for (int k = 0; k < K_STEPS; ++k) {
                         const uint64_t koff = static_cast<uint64_t>((k * UMMA_K_BYTES) >> 4);
                         const uint32_t acc = (kb | k) != 0;
-                        if (KIND == RKB_IN_F16) tc_mma_f16(dcol, adesc + koff, bdesc + koff, IDESC, acc);
-                        else                    tc_mma_i8(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                        if (KIND == RKB_IN_I8)        tc_mma_i8(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                        else if (KIND == RKB_IN_TF32) tc_mma_tf32(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                        else                          tc_mma_f16(dcol, adesc + koff, bdesc + koff, IDESC, acc);
                     }
                     tc_commit(empty_bar(s));
                     if (++s == STAGES) { s = 0; ph ^= 1; }
@@ -287,9 +310,8 @@ int launch(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
         cudaFuncSetAttribute(gemm_kernel<KIND, OUT, BN>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     });
-    const int esize = (KIND == RKB_IN_F16) ? 2 : 1;
-    const CUtensorMapDataType dt =
-        (KIND == RKB_IN_F16) ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    const int esize = Kind<KIND>::ESIZE;
+    const CUtensorMapDataType dt = Kind<KIND>::DT;
     CUtensorMap ta, tb;
     if (make_tmap_2d(&ta, d->A, dt, esize, d->K, d->M, d->lda, BK_BYTES / esize, BM) ||
         make_tmap_2d(&tb, d->B, dt, esize, d->K, d->N, d->ldb, BK_BYTES / esize, BN))
@@ -344,9 +366,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
              const Args g) {
     using C = Cfg2<BN>;
     constexpr int STAGES = C::STAGES;
-    constexpr int BK_ELEMS = (KIND == RKB_IN_F16) ? 64 : 128;
-    constexpr uint32_t IDESC = (KIND == RKB_IN_F16) ? idesc_f16_f32acc(2 * BM, BN)
-                                                    : idesc_s8_s32acc(2 * BM, BN);
+    constexpr int BK_ELEMS = BK_BYTES / Kind<KIND>::ESIZE;
+    constexpr uint32_t IDESC = Kind<KIND>::idesc(2 * BM, BN);
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -446,8 +467,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
                     for (int k = 0; k < 4; ++k) {
                         const uint64_t koff = static_cast<uint64_t>((k * 32) >> 4);
                         const uint32_t acc = (kb != kb0) || (k != 0);
-                        if (KIND == RKB_IN_F16) tc_mma_f16_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
-                        else                    tc_mma_i8_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                        if (KIND == RKB_IN_I8)        tc_mma_i8_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                        else if (KIND == RKB_IN_TF32) tc_mma_tf32_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                        else                          tc_mma_f16_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
                     }
                     tc_commit_pair(empty_bar(s));
                     tc_commit_pair(mapa_shared(empty_bar(s), peer));
@@ -512,9 +534,8 @@ int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream, int splits = 
         cudaFuncSetAttribute(gemm2_kernel<KIND, OUT, BN>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     });
-    const int esize = (KIND == RKB_IN_F16) ? 2 : 1;
-    const CUtensorMapDataType dt =
-        (KIND == RKB_IN_F16) ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    const int esize = Kind<KIND>::ESIZE;
+    const CUtensorMapDataType dt = Kind<KIND>::DT;
     CUtensorMap ta, tb;
     if (make_tmap_2d(&ta, d->A, dt, esize, d->K, d->M, d->lda, BK_BYTES / esize, BM) ||
         make_tmap_2d(&tb, d->B, dt, esize, d->K, d->N, d->ldb, BK_BYTES / esize, C::BNH))
@@ -628,7 +649,7 @@ inline int pick_splits(const rkb_gemm_desc *d) {
     if (!e) return 1;
     int s = atoi(e);
     const int kblocks = (d->K * 2 + BK_BYTES - 1) / BK_BYTES;
-    if (s > 4) s = 4;
+    if (s > 4) s = 4;   // (fp16 only)
     while (s > 1 && kblocks / s < 4) --s;
     return s < 1 ? 1 : s;
 }
@@ -677,6 +698,10 @@ extern "C" int rkb_gemm_run(const rkb_gemm_desc *d, int *err, cudaStream_t strea
         if (d->out_kind == RKB_OUT_F32) { RKB_DISPATCH(RKB_IN_F16, RKB_OUT_F32); }
     } else if (d->in_kind == RKB_IN_I8) {
         if (d->out_kind == RKB_OUT_I32) { RKB_DISPATCH(RKB_IN_I8, RKB_OUT_I32); }
+    } else if (d->in_kind == RKB_IN_BF16) {
+        if (d->out_kind == RKB_OUT_F32) { RKB_DISPATCH(RKB_IN_BF16, RKB_OUT_F32); }
+    } else if (d->in_kind == RKB_IN_TF32) {
+        if (d->out_kind == RKB_OUT_F32) { RKB_DISPATCH(RKB_IN_TF32, RKB_OUT_F32); }
     }
 #undef RKB_DISPATCH
     return ROCKET_E_UNSUPPORTED;

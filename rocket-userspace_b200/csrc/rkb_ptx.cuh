@@ -166,6 +166,13 @@ RKB_DEV void tc_mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
         ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accum) : "memory");
 }
+// D(tmem) (+)= A * B^T, tf32 inputs (fp32 storage), fp32 accumulate.
+RKB_DEV void tc_mma_tf32(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n"
+        ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accum) : "memory");
+}
 // D(tmem) (+)= A * B^T, signed/unsigned 8-bit inputs, int32 accumulate.
 RKB_DEV void tc_mma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
     asm volatile(
@@ -245,6 +252,12 @@ RKB_DEV void tc_mma_f16_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
         "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
         ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accum) : "memory");
 }
+RKB_DEV void tc_mma_tf32_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n"
+        ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accum) : "memory");
+}
 RKB_DEV void tc_mma_i8_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -275,6 +288,11 @@ RKB_DEV uint64_t smem_desc_sw128(uint32_t saddr) {
 //   (f16: 0 = f16, 1 = bf16; i8: 1 = signed), bits 17-22 N >> 3, bits 24-28 M >> 4.
 __host__ __device__ constexpr uint32_t idesc_f16_f32acc(int m, int n) {
     return (1u << 4) | (0u << 7) | (0u << 10) |
+           (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+// kind::f16 with bf16 operands (format 1) / kind::tf32 (format 2), fp32 accumulate
+__host__ __device__ constexpr uint32_t idesc_f32acc_fmt(int fmt, int m, int n) {
+    return (1u << 4) | (static_cast<uint32_t>(fmt) << 7) | (static_cast<uint32_t>(fmt) << 10) |
            (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 __host__ __device__ constexpr uint32_t idesc_s8_s32acc(int m, int n) {

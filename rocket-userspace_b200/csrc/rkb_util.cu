@@ -171,3 +171,56 @@ int rkb_device_sm_count(int dev) {
 }
 
 }  // extern "C"
+
+// ---- dtype helpers for the bf16 / int16 matmul entries -----------------------
+namespace {
+
+// fp32 -> bf16 by truncation of the low 16 bits (the reference's bf16 pack
+// drops them, include/rocket_matmul.h:510-513)
+__global__ void f32_to_bf16_trunc(const uint32_t *__restrict__ src, size_t n, uint16_t *__restrict__ dst) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        dst[i] = static_cast<uint16_t>(src[i] >> 16);
+}
+
+// int16 -> (hi, lo) signed bytes with v = 256*hi + lo, v clamped to [-32768, 32639]
+// (the reference's exact int16 route, include/rocket_matmul.h:489-499)
+__global__ void int16_split(const int16_t *__restrict__ src, size_t n, int8_t *__restrict__ hi,
+                            int8_t *__restrict__ lo) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        int v = src[i];
+        if (v > 32639) v = 32639;
+        const int h = (v + 128) >> 8;          // arithmetic shift = floor division
+        hi[i] = static_cast<int8_t>(h);
+        lo[i] = static_cast<int8_t>(v - 256 * h);
+    }
+}
+
+// C = 65536*hh + 256*(hl + lh) + ll in int64
+__global__ void int16_combine(const int32_t *__restrict__ hh, const int32_t *__restrict__ hl,
+                              const int32_t *__restrict__ lh, const int32_t *__restrict__ ll, size_t n,
+                              int64_t *__restrict__ out) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        out[i] = 65536ll * hh[i] + 256ll * (static_cast<int64_t>(hl[i]) + lh[i]) + ll[i];
+}
+
+}  // namespace
+
+extern "C" int rkb_f32_to_bf16(const void *src, size_t n, void *dst, cudaStream_t s) {
+    f32_to_bf16_trunc<<<grid_for(n, 256), 256, 0, s>>>(static_cast<const uint32_t *>(src), n,
+                                                       static_cast<uint16_t *>(dst));
+    return status(cudaGetLastError());
+}
+
+extern "C" int rkb_int16_split(const int16_t *src, size_t n, int8_t *hi, int8_t *lo, cudaStream_t s) {
+    int16_split<<<grid_for(n, 256), 256, 0, s>>>(src, n, hi, lo);
+    return status(cudaGetLastError());
+}
+
+extern "C" int rkb_int16_combine(const int32_t *hh, const int32_t *hl, const int32_t *lh, const int32_t *ll,
+                                 size_t n, int64_t *out, cudaStream_t s) {
+    int16_combine<<<grid_for(n, 256), 256, 0, s>>>(hh, hl, lh, ll, n, out);
+    return status(cudaGetLastError());
+}

@@ -233,6 +233,75 @@ __global__ void split_heads(const __half *__restrict__ qkv, long ld, int B, int 
     }
 }
 
+// out[m] = sum (or mean) of row m, fp32 (src/rocket_reduce.c:380-390 definition)
+__global__ void reduce_rows(const __half *__restrict__ x, int M, int H, int mean, float *__restrict__ out) {
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    const bool vec = (H % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+        RowView r{x + static_cast<size_t>(row) * H, H, vec};
+        float s = 0.f;
+        row_for_each(r, lane, [&](int, float v) { s += v; });
+        s = warp_sum(s);
+        if (lane == 0) out[row] = mean ? s / H : s;
+    }
+}
+
+// Inclusive / exclusive, forward / reverse prefix sums per row (fp32 running
+// sum, fp16 store): one warp per row, 32-element chunks, shuffle scan + carry
+// (src/rocket_reduce.c:445-464 definition).
+__global__ void cumsum_rows(const __half *__restrict__ x, int M, int N, int exclusive, int reverse,
+                            __half *__restrict__ out) {
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+        const __half *xr = x + static_cast<size_t>(row) * N;
+        __half *orow = out + static_cast<size_t>(row) * N;
+        float carry = 0.f;
+        for (int base = 0; base < N; base += 32) {
+            const int j = base + lane;
+            const int idx = reverse ? N - 1 - j : j;
+            const float v = (j < N) ? __half2float(xr[idx]) : 0.f;
+            float incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += t;
+            }
+            if (j < N) orow[idx] = __float2half_rn(carry + (exclusive ? incl - v : incl));
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+    }
+}
+
+// out[m, n] = in[m, n] * r[m] (src/rocket_norm.c:21-30 definition)
+__global__ void scale_rows(const __half *__restrict__ x, const float *__restrict__ r, int M, int N,
+                           __half *__restrict__ out) {
+    const size_t total = static_cast<size_t>(M) * N;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        out[i] = __float2half_rn(__half2float(x[i]) * r[i / N]);
+}
+
+// loss[m] = logsumexp(row m) - row[m][target[m]] (src/rocket_softmax.c:141-155 definition)
+__global__ void cross_entropy_rows(const __half *__restrict__ x, const int *__restrict__ target, int M,
+                                   int N, float *__restrict__ loss) {
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    const bool vec = (N % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+        RowView r{x + static_cast<size_t>(row) * N, N, vec};
+        float mx = -INFINITY;
+        row_for_each(r, lane, [&](int, float v) { mx = fmaxf(mx, v); });
+        mx = warp_max(mx);
+        float s = 0.f;
+        row_for_each(r, lane, [&](int, float v) { s += expf(v - mx); });
+        s = warp_sum(s);
+        if (lane == 0) {
+            const int t = target[row];
+            const float g = (t >= 0 && t < N) ? __half2float(r.p[t]) : 0.f;
+            loss[row] = mx + logf(s) - g;
+        }
+    }
+}
+
 int grid_for(size_t work, int threads) {
     size_t b = (work + threads - 1) / threads;
     if (b > 148 * 32) b = 148 * 32;
@@ -275,6 +344,38 @@ int rkb_elementwise(const void *a, const void *b, int op, int kind, size_t n, vo
     elementwise<<<grid_for(n / 8 + 1, 256), 256, 0, s>>>(static_cast<const __half *>(a),
                                                          static_cast<const __half *>(b), op, kind, n,
                                                          static_cast<__half *>(out));
+    return status();
+}
+
+int rkb_reduce_rows(const void *x, int M, int H, int mean, float *out, cudaStream_t s) {
+    if (M <= 0 || H <= 0) return ROCKET_E_SHAPE;
+    int grid = (M + 7) / 8;
+    if (grid > 148 * 16) grid = 148 * 16;
+    reduce_rows<<<grid, 256, 0, s>>>(static_cast<const __half *>(x), M, H, mean, out);
+    return status();
+}
+
+int rkb_cumsum_rows(const void *x, int M, int N, int exclusive, int reverse, void *out, cudaStream_t s) {
+    if (M <= 0 || N <= 0) return ROCKET_E_SHAPE;
+    int grid = (M + 7) / 8;
+    if (grid > 148 * 16) grid = 148 * 16;
+    cumsum_rows<<<grid, 256, 0, s>>>(static_cast<const __half *>(x), M, N, exclusive, reverse,
+                                     static_cast<__half *>(out));
+    return status();
+}
+
+int rkb_scale_rows(const void *x, const float *r, int M, int N, void *out, cudaStream_t s) {
+    if (M <= 0 || N <= 0) return ROCKET_E_SHAPE;
+    scale_rows<<<grid_for(static_cast<size_t>(M) * N, 256), 256, 0, s>>>(static_cast<const __half *>(x), r, M, N,
+                                                                          static_cast<__half *>(out));
+    return status();
+}
+
+int rkb_cross_entropy_rows(const void *x, const int *target, int M, int N, float *loss, cudaStream_t s) {
+    if (M <= 0 || N <= 0) return ROCKET_E_SHAPE;
+    int grid = (M + 7) / 8;
+    if (grid > 148 * 16) grid = 148 * 16;
+    cross_entropy_rows<<<grid, 256, 0, s>>>(static_cast<const __half *>(x), target, M, N, loss);
     return status();
 }
 

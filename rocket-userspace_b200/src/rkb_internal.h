@@ -98,8 +98,37 @@ int rkb_gw_on(rkb_handle *h, int M, int N, int K, int group, int w_bits,
               const int8_t *dA, const float *a_scale, int a_rows_const,
               const void *dWq, const float *b_scale, void *dC, long ldc, int out_kind);
 
+/* One dense GEMM call on operands anywhere (staged as needed).  finish = 0
+ * leaves the call queued on the handle's stream for a later rkb_finish. */
+int rkb_oneshot_dense(const char *who, int fd, int in_kind, int out_kind, int M, int K, int N,
+                      const void *A, const void *B, void *C, int finish);
+
 /* 1 if a host-resident a_scale [M*nG] is constant along g for every row. */
 int rkb_rows_const(const float *a_scale, int M, int nG);
+
+/* ---- composite-call plumbing (rkb_call.c) ---- */
+#define RKB_CALL_MAX_TMP 64
+typedef struct {
+    rkb_handle *h;
+    const char *who;
+    void *tmp[RKB_CALL_MAX_TMP];
+    int ntmp;
+    int rc;
+    struct { void *user; const void *dev; size_t bytes; } outs[4];
+    int nouts;
+} rkb_call;
+int         rkb_call_begin(rkb_call *c, int fd, const char *who);
+void       *rkb_call_tmp(rkb_call *c, size_t bytes);                      /* stream-ordered temporary */
+const void *rkb_call_in(rkb_call *c, const void *user, size_t bytes);    /* device view of an input */
+void       *rkb_call_out(rkb_call *c, void *user, size_t bytes);         /* device buffer for an output */
+void        rkb_call_check(rkb_call *c, int rc);
+int         rkb_call_end(rkb_call *c);                                   /* copy back, free, bounded wait */
+/* fp16-input GEMM with fused epilogue: C = act(A W^T + bias) + residual (fp16 out) */
+void        rkb_call_gemm(rkb_call *c, int M, int N, int K, const void *A, long lda, const void *W,
+                          void *C, long ldc, const void *bias, int act, const void *res, long ldr);
+/* any-kind GEMM on device operands with the call's temporaries for workspace */
+void        rkb_call_gemm_kind(rkb_call *c, int in_kind, int out_kind, int M, int N, int K,
+                               const void *A, long lda, const void *B, long ldb, void *C, long ldc);
 
 /* Environment helpers (read on each call; cheap). */
 long rkb_env_long(const char *name, long dflt);

@@ -15,7 +15,7 @@
 extern "C" {
 #endif
 
-enum rkb_in_kind  { RKB_IN_F16 = 0, RKB_IN_I8 = 1 };
+enum rkb_in_kind  { RKB_IN_F16 = 0, RKB_IN_I8 = 1, RKB_IN_BF16 = 2, RKB_IN_TF32 = 3 };
 enum rkb_out_kind { RKB_OUT_F16 = 0, RKB_OUT_I32 = 1, RKB_OUT_F32 = 2 };
 
 /* Dense C[M,N] = A[M,K] * B[N,K]^T on tcgen05.  Leading dimensions are in
@@ -103,6 +103,17 @@ int rkb_split_heads(const void *qkv, long ld, int B, int T, int Tp, int H, int d
 /* out[b*T + t, h*dh + c] = softmax(Q K^T * scale) V per (b, h); dh == 64, Tp % 128 == 0 */
 int rkb_attention(const void *Q, const void *K, const void *Vt, int B, int H, int T, int Tp,
                   int dh, float scale, void *out, long ldo, int *err, cudaStream_t stream);
+
+int rkb_reduce_rows(const void *x, int M, int H, int mean, float *out, cudaStream_t s);
+int rkb_cumsum_rows(const void *x, int M, int N, int exclusive, int reverse, void *out, cudaStream_t s);
+int rkb_scale_rows(const void *x, const float *r, int M, int N, void *out, cudaStream_t s);
+int rkb_cross_entropy_rows(const void *x, const int *target, int M, int N, float *loss, cudaStream_t s);
+
+/* ---- dtype helpers (csrc/rkb_util.cu) ---- */
+int rkb_f32_to_bf16(const void *src, size_t n, void *dst, cudaStream_t s);     /* truncating */
+int rkb_int16_split(const int16_t *src, size_t n, int8_t *hi, int8_t *lo, cudaStream_t s);
+int rkb_int16_combine(const int32_t *hh, const int32_t *hl, const int32_t *lh, const int32_t *ll,
+                      size_t n, int64_t *out, cudaStream_t s);
 
 /* Device properties cached per device. */
 int rkb_device_sm_count(int dev);

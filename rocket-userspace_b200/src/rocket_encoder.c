@@ -24,122 +24,9 @@
 #include "rocket_encoder.h"
 #include "rocket_ffn.h"
 #include "rocket_norm.h"
+#include "rocket_reduce.h"
 #include "rocket_softmax.h"
 #include "rkb_internal.h"
-
-#define ENC_MAX_TMP 48
-
-typedef struct {
-    rkb_handle *h;
-    const char *who;
-    void *tmp[ENC_MAX_TMP];
-    int ntmp;
-    int rc;
-    struct { void *user; const void *dev; size_t bytes; } outs[4];
-    int nouts;
-} enc_call;
-
-static int enc_begin(enc_call *c, int fd, const char *who)
-{
-    memset(c, 0, sizeof *c);
-    c->who = who;
-    c->h = rkb_get(fd);
-    if (!c->h) {
-        ROCKET_LOGE("%s: bad device handle %d\n", who, fd);
-        return ROCKET_E_DEVICE;
-    }
-    static int pool_ready[64];
-    int dev = c->h->device;
-    if (dev < 64 && !pool_ready[dev]) {
-        cudaMemPool_t pool;
-        if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
-            uint64_t thr = UINT64_MAX;
-            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
-        }
-        cudaGetLastError();
-        pool_ready[dev] = 1;
-    }
-    return 0;
-}
-
-static void *enc_tmp(enc_call *c, size_t bytes)
-{
-    if (c->rc || c->ntmp >= ENC_MAX_TMP) { if (!c->rc) c->rc = ROCKET_E_NOMEM; return NULL; }
-    void *p = NULL;
-    if (cudaMallocAsync(&p, bytes ? bytes : 16, c->h->stream) != cudaSuccess) {
-        cudaGetLastError();
-        c->rc = ROCKET_E_NOMEM;
-        return NULL;
-    }
-    c->tmp[c->ntmp++] = p;
-    return p;
-}
-
-/* device view of a caller input (NULL stays NULL) */
-static const void *enc_in(enc_call *c, const void *user, size_t bytes)
-{
-    if (!user || c->rc) return NULL;
-    if (rkb_ptr_device(user) == c->h->device && ((uintptr_t)user & 15) == 0) return user;
-    void *d = enc_tmp(c, bytes);
-    if (d && cudaMemcpyAsync(d, user, bytes, cudaMemcpyDefault, c->h->stream) != cudaSuccess) {
-        cudaGetLastError();
-        c->rc = ROCKET_E_DEVICE;
-    }
-    return d;
-}
-
-/* device buffer for a caller output; copied back in enc_end when needed */
-static void *enc_out(enc_call *c, void *user, size_t bytes)
-{
-    if (c->rc) return NULL;
-    if (rkb_ptr_device(user) == c->h->device && ((uintptr_t)user & 15) == 0) return user;
-    void *d = enc_tmp(c, bytes);
-    if (d && c->nouts < 4) {
-        c->outs[c->nouts].user = user;
-        c->outs[c->nouts].dev = d;
-        c->outs[c->nouts].bytes = bytes;
-        c->nouts++;
-    }
-    return d;
-}
-
-static void enc_check(enc_call *c, int rc)
-{
-    if (!c->rc && rc) c->rc = rc;
-}
-
-static int enc_end(enc_call *c)
-{
-    for (int i = 0; i < c->nouts && !c->rc; i++)
-        if (cudaMemcpyAsync(c->outs[i].user, c->outs[i].dev, c->outs[i].bytes, cudaMemcpyDefault,
-                            c->h->stream) != cudaSuccess) {
-            cudaGetLastError();
-            c->rc = ROCKET_E_DEVICE;
-        }
-    for (int i = 0; i < c->ntmp; i++) cudaFreeAsync(c->tmp[i], c->h->stream);
-    rkb_count(1, 0);
-    int fr = rkb_finish(c->h, c->who);
-    return c->rc ? c->rc : fr;
-}
-
-/* GEMM with fp16 output and fused epilogue: C = act(A W^T + bias) + residual */
-static void enc_gemm(enc_call *c, int M, int N, int K, const void *A, long lda, const void *W,
-                     void *C, long ldc, const void *bias, int act, const void *res, long ldr)
-{
-    if (c->rc) return;
-    rkb_gemm_desc d;
-    memset(&d, 0, sizeof d);
-    d.in_kind = RKB_IN_F16; d.out_kind = RKB_OUT_F16;
-    d.M = M; d.N = N; d.K = K;
-    d.A = A; d.lda = lda; d.B = W; d.ldb = K; d.C = C; d.ldc = ldc;
-    d.bias = bias; d.act = act; d.residual = res; d.ldr = ldr;
-    const size_t wb = rkb_gemm_workspace_bytes(&d);
-    if (wb && !(d.workspace = enc_tmp(c, wb))) return;
-    rkb_count(0, wb ? 2 : 1);
-    int ps = rkb_prof_begin(c->h);
-    enc_check(c, rkb_gemm_run(&d, c->h->err_dev, c->h->stream));
-    rkb_prof_end(c->h, ps, RKB_K_GEMM_F16);
-}
 
 static int epi_act(int kind)
 {
@@ -153,21 +40,21 @@ static int norm_common(const char *who, int fd, int M, int H, const void *x, con
                        const void *b, float eps, int rms, void *out)
 {
     if (M < 1 || H < 1 || !x || !g || !out) return ROCKET_E_SHAPE;
-    enc_call c;
-    int rc = enc_begin(&c, fd, who);
+    rkb_call c;
+    int rc = rkb_call_begin(&c, fd, who);
     if (rc) return rc;
     const size_t bytes = (size_t)M * H * 2;
-    const void *dx = enc_in(&c, x, bytes);
-    const void *dg = enc_in(&c, g, (size_t)H * 2);
-    const void *db = enc_in(&c, b, (size_t)H * 2);
-    void *dout = enc_out(&c, out, bytes);
+    const void *dx = rkb_call_in(&c, x, bytes);
+    const void *dg = rkb_call_in(&c, g, (size_t)H * 2);
+    const void *db = rkb_call_in(&c, b, (size_t)H * 2);
+    void *dout = rkb_call_out(&c, out, bytes);
     if (!c.rc) {
         int ps = rkb_prof_begin(c.h);
-        enc_check(&c, rkb_norm_rows(dx, dg, db, M, H, eps, rms, dout, c.h->stream));
+        rkb_call_check(&c, rkb_norm_rows(dx, dg, db, M, H, eps, rms, dout, c.h->stream));
         rkb_prof_end(c.h, ps, RKB_K_NORM);
         rkb_count(0, 1);
     }
-    return enc_end(&c);
+    return rkb_call_end(&c);
 }
 
 int rocket_layernorm_fp16(int fd, int M, int H, const _Float16 *x, const _Float16 *gamma,
@@ -185,19 +72,19 @@ int rocket_rmsnorm_fp16(int fd, int M, int H, const _Float16 *x, const _Float16 
 static int softmax_common(const char *who, int fd, int M, int N, const void *in, void *out, int lg)
 {
     if (M < 1 || N < 1 || !in || !out) return ROCKET_E_SHAPE;
-    enc_call c;
-    int rc = enc_begin(&c, fd, who);
+    rkb_call c;
+    int rc = rkb_call_begin(&c, fd, who);
     if (rc) return rc;
     const size_t bytes = (size_t)M * N * 2;
-    const void *dx = enc_in(&c, in, bytes);
-    void *dout = enc_out(&c, out, bytes);
+    const void *dx = rkb_call_in(&c, in, bytes);
+    void *dout = rkb_call_out(&c, out, bytes);
     if (!c.rc) {
         int ps = rkb_prof_begin(c.h);
-        enc_check(&c, rkb_softmax_rows(dx, M, N, lg, dout, c.h->stream));
+        rkb_call_check(&c, rkb_softmax_rows(dx, M, N, lg, dout, c.h->stream));
         rkb_prof_end(c.h, ps, RKB_K_SOFTMAX);
         rkb_count(0, 1);
     }
-    return enc_end(&c);
+    return rkb_call_end(&c);
 }
 
 int rocket_softmax_fp16(int fd, int M, int N, const _Float16 *in, _Float16 *out)
@@ -215,20 +102,20 @@ static int ew_common(const char *who, int fd, const void *a, const void *b, int 
                      void *out, int n)
 {
     if (n <= 0 || !a || !out || (op && !b)) return ROCKET_E_SHAPE;
-    enc_call c;
-    int rc = enc_begin(&c, fd, who);
+    rkb_call c;
+    int rc = rkb_call_begin(&c, fd, who);
     if (rc) return rc;
     const size_t bytes = (size_t)n * 2;
-    const void *da = enc_in(&c, a, bytes);
-    const void *db = op ? enc_in(&c, b, bytes) : NULL;
-    void *dout = enc_out(&c, out, bytes);
+    const void *da = rkb_call_in(&c, a, bytes);
+    const void *db = op ? rkb_call_in(&c, b, bytes) : NULL;
+    void *dout = rkb_call_out(&c, out, bytes);
     if (!c.rc) {
         int ps = rkb_prof_begin(c.h);
-        enc_check(&c, rkb_elementwise(da, db, op, kind, (size_t)n, dout, c.h->stream));
+        rkb_call_check(&c, rkb_elementwise(da, db, op, kind, (size_t)n, dout, c.h->stream));
         rkb_prof_end(c.h, ps, RKB_K_ELEMWISE);
         rkb_count(0, 1);
     }
-    return enc_end(&c);
+    return rkb_call_end(&c);
 }
 
 static int kind_ok(int kind)
@@ -275,25 +162,25 @@ int rocket_ffn_fp16(int fd, int M, int H, int I, const _Float16 *x, const _Float
     if (M < 1 || H < 1 || I < 1 || H % 32 || I % 32 || M % 4 || !x || !Wg || !Wu || !Wd || !out)
         return ROCKET_E_SHAPE;
     if (!kind_ok(kind)) return ROCKET_E_UNSUPPORTED;
-    enc_call c;
-    int rc = enc_begin(&c, fd, who);
+    rkb_call c;
+    int rc = rkb_call_begin(&c, fd, who);
     if (rc) return rc;
-    const void *dx = enc_in(&c, x, (size_t)M * H * 2);
-    const void *dwg = enc_in(&c, Wg, (size_t)I * H * 2);
-    const void *dwu = enc_in(&c, Wu, (size_t)I * H * 2);
-    const void *dwd = enc_in(&c, Wd, (size_t)H * I * 2);
-    void *gate = enc_tmp(&c, (size_t)M * I * 2);
-    void *up = enc_tmp(&c, (size_t)M * I * 2);
-    void *dout = enc_out(&c, out, (size_t)M * H * 2);
-    enc_gemm(&c, M, I, H, dx, H, dwg, gate, I, NULL, RKB_ACT_NONE, NULL, 0);
-    enc_gemm(&c, M, I, H, dx, H, dwu, up, I, NULL, RKB_ACT_NONE, NULL, 0);
+    const void *dx = rkb_call_in(&c, x, (size_t)M * H * 2);
+    const void *dwg = rkb_call_in(&c, Wg, (size_t)I * H * 2);
+    const void *dwu = rkb_call_in(&c, Wu, (size_t)I * H * 2);
+    const void *dwd = rkb_call_in(&c, Wd, (size_t)H * I * 2);
+    void *gate = rkb_call_tmp(&c, (size_t)M * I * 2);
+    void *up = rkb_call_tmp(&c, (size_t)M * I * 2);
+    void *dout = rkb_call_out(&c, out, (size_t)M * H * 2);
+    rkb_call_gemm(&c, M, I, H, dx, H, dwg, gate, I, NULL, RKB_ACT_NONE, NULL, 0);
+    rkb_call_gemm(&c, M, I, H, dx, H, dwu, up, I, NULL, RKB_ACT_NONE, NULL, 0);
     if (!c.rc) {
         int ps = rkb_prof_begin(c.h);
-        enc_check(&c, rkb_elementwise(gate, up, 4, kind, (size_t)M * I, gate, c.h->stream));
+        rkb_call_check(&c, rkb_elementwise(gate, up, 4, kind, (size_t)M * I, gate, c.h->stream));
         rkb_prof_end(c.h, ps, RKB_K_ELEMWISE);
     }
-    enc_gemm(&c, M, H, I, gate, I, dwd, dout, H, NULL, RKB_ACT_NONE, NULL, 0);
-    return enc_end(&c);
+    rkb_call_gemm(&c, M, H, I, gate, I, dwd, dout, H, NULL, RKB_ACT_NONE, NULL, 0);
+    return rkb_call_end(&c);
 }
 
 int rocket_ffn_fp16_fused(int fd, int M, int H, int I, const _Float16 *x, const _Float16 *Wg,
@@ -311,44 +198,44 @@ int rocket_mlp_fp16_fused(int fd, int M, int Din, int Dff, int Dout, const _Floa
         !x || !W1 || !W2 || !out)
         return ROCKET_E_SHAPE;
     if (!kind_ok(kind)) return ROCKET_E_UNSUPPORTED;
-    enc_call c;
-    int rc = enc_begin(&c, fd, who);
+    rkb_call c;
+    int rc = rkb_call_begin(&c, fd, who);
     if (rc) return rc;
-    const void *dx = enc_in(&c, x, (size_t)M * Din * 2);
-    const void *dw1 = enc_in(&c, W1, (size_t)Dff * Din * 2);
-    const void *db1 = enc_in(&c, b1, (size_t)Dff * 2);
-    const void *dw2 = enc_in(&c, W2, (size_t)Dout * Dff * 2);
-    void *f1 = enc_tmp(&c, (size_t)M * Dff * 2);
-    void *dout = enc_out(&c, out, (size_t)M * Dout * 2);
+    const void *dx = rkb_call_in(&c, x, (size_t)M * Din * 2);
+    const void *dw1 = rkb_call_in(&c, W1, (size_t)Dff * Din * 2);
+    const void *db1 = rkb_call_in(&c, b1, (size_t)Dff * 2);
+    const void *dw2 = rkb_call_in(&c, W2, (size_t)Dout * Dff * 2);
+    void *f1 = rkb_call_tmp(&c, (size_t)M * Dff * 2);
+    void *dout = rkb_call_out(&c, out, (size_t)M * Dout * 2);
     const int ea = epi_act(kind);
-    enc_gemm(&c, M, Dff, Din, dx, Din, dw1, f1, Dff, db1, ea < 0 ? RKB_ACT_NONE : ea, NULL, 0);
-    if (ea < 0 && !c.rc) enc_check(&c, rkb_elementwise(f1, NULL, 0, kind, (size_t)M * Dff, f1, c.h->stream));
-    enc_gemm(&c, M, Dout, Dff, f1, Dff, dw2, dout, Dout, NULL, RKB_ACT_NONE, NULL, 0);
-    return enc_end(&c);
+    rkb_call_gemm(&c, M, Dff, Din, dx, Din, dw1, f1, Dff, db1, ea < 0 ? RKB_ACT_NONE : ea, NULL, 0);
+    if (ea < 0 && !c.rc) rkb_call_check(&c, rkb_elementwise(f1, NULL, 0, kind, (size_t)M * Dff, f1, c.h->stream));
+    rkb_call_gemm(&c, M, Dout, Dff, f1, Dff, dw2, dout, Dout, NULL, RKB_ACT_NONE, NULL, 0);
+    return rkb_call_end(&c);
 }
 
 /* ---- attention ------------------------------------------------------------------------- */
 /* ctx[nb*T, d] = MHA core over nb sequences from ln[nb*T, d] (q/k/v projections included) */
-static void enc_mha_core(enc_call *c, int nb, int T, int d, int n_head, const void *ln,
+static void enc_mha_core(rkb_call *c, int nb, int T, int d, int n_head, const void *ln,
                          const void *Wq, const void *bq, const void *Wk, const void *bk,
                          const void *Wv, const void *bv, void *ctx)
 {
     if (c->rc) return;
     const int BT = nb * T, dh = d / n_head, Tp = (T + 127) / 128 * 128;
-    void *qkv = enc_tmp(c, (size_t)BT * 3 * d * 2);
+    void *qkv = rkb_call_tmp(c, (size_t)BT * 3 * d * 2);
     const size_t hsz = (size_t)nb * n_head * Tp * dh * 2;
-    void *Q = enc_tmp(c, hsz), *K = enc_tmp(c, hsz), *Vt = enc_tmp(c, hsz);
+    void *Q = rkb_call_tmp(c, hsz), *K = rkb_call_tmp(c, hsz), *Vt = rkb_call_tmp(c, hsz);
     if (c->rc) return;
-    enc_gemm(c, BT, d, d, ln, d, Wq, qkv, 3 * d, bq, RKB_ACT_NONE, NULL, 0);
-    enc_gemm(c, BT, d, d, ln, d, Wk, (uint8_t *)qkv + (size_t)d * 2, 3 * d, bk, RKB_ACT_NONE, NULL, 0);
-    enc_gemm(c, BT, d, d, ln, d, Wv, (uint8_t *)qkv + (size_t)2 * d * 2, 3 * d, bv, RKB_ACT_NONE, NULL, 0);
+    rkb_call_gemm(c, BT, d, d, ln, d, Wq, qkv, 3 * d, bq, RKB_ACT_NONE, NULL, 0);
+    rkb_call_gemm(c, BT, d, d, ln, d, Wk, (uint8_t *)qkv + (size_t)d * 2, 3 * d, bk, RKB_ACT_NONE, NULL, 0);
+    rkb_call_gemm(c, BT, d, d, ln, d, Wv, (uint8_t *)qkv + (size_t)2 * d * 2, 3 * d, bv, RKB_ACT_NONE, NULL, 0);
     if (c->rc) return;
     int ps = rkb_prof_begin(c->h);
-    enc_check(c, rkb_split_heads(qkv, 3 * d, nb, T, Tp, n_head, dh, Q, K, Vt, c->h->stream));
+    rkb_call_check(c, rkb_split_heads(qkv, 3 * d, nb, T, Tp, n_head, dh, Q, K, Vt, c->h->stream));
     rkb_prof_end(c->h, ps, RKB_K_ELEMWISE);
     ps = rkb_prof_begin(c->h);
     if (!c->rc)
-        enc_check(c, rkb_attention(Q, K, Vt, nb, n_head, T, Tp, dh, 1.0f / sqrtf((float)dh), ctx, d,
+        rkb_call_check(c, rkb_attention(Q, K, Vt, nb, n_head, T, Tp, dh, 1.0f / sqrtf((float)dh), ctx, d,
                                    c->h->err_dev, c->h->stream));
     rkb_prof_end(c->h, ps, RKB_K_ATTN);
     rkb_count(0, 2);
@@ -370,18 +257,18 @@ int rocket_mha_self_fp16(int fd, int T, int d, int n_head, const _Float16 *x, co
         ROCKET_LOGE("%s: head_dim %d unsupported (the fused kernel is built for 64)\n", who, d / n_head);
         return ROCKET_E_UNSUPPORTED;
     }
-    enc_call c;
-    int rc = enc_begin(&c, fd, who);
+    rkb_call c;
+    int rc = rkb_call_begin(&c, fd, who);
     if (rc) return rc;
     const size_t w = (size_t)d * d * 2, v = (size_t)d * 2, a = (size_t)T * d * 2;
-    const void *dx = enc_in(&c, x, a);
-    const void *dq = enc_in(&c, Wq, w), *dk = enc_in(&c, Wk, w), *dv = enc_in(&c, Wv, w), *dwo = enc_in(&c, Wo, w);
-    const void *dbq = enc_in(&c, bq, v), *dbk = enc_in(&c, bk, v), *dbv = enc_in(&c, bv, v), *dbo = enc_in(&c, bo, v);
-    void *ctx = enc_tmp(&c, a);
-    void *dout = enc_out(&c, out, a);
+    const void *dx = rkb_call_in(&c, x, a);
+    const void *dq = rkb_call_in(&c, Wq, w), *dk = rkb_call_in(&c, Wk, w), *dv = rkb_call_in(&c, Wv, w), *dwo = rkb_call_in(&c, Wo, w);
+    const void *dbq = rkb_call_in(&c, bq, v), *dbk = rkb_call_in(&c, bk, v), *dbv = rkb_call_in(&c, bv, v), *dbo = rkb_call_in(&c, bo, v);
+    void *ctx = rkb_call_tmp(&c, a);
+    void *dout = rkb_call_out(&c, out, a);
     enc_mha_core(&c, 1, T, d, n_head, dx, dq, dbq, dk, dbk, dv, dbv, ctx);
-    enc_gemm(&c, T, d, d, ctx, d, dwo, dout, d, dbo, RKB_ACT_NONE, NULL, 0);
-    return enc_end(&c);
+    rkb_call_gemm(&c, T, d, d, ctx, d, dwo, dout, d, dbo, RKB_ACT_NONE, NULL, 0);
+    return rkb_call_end(&c);
 }
 
 /* ---- encoder block ------------------------------------------------------------------- */
@@ -399,37 +286,37 @@ static int encoder_common(const char *who, int fd, int nb, int T, int d, int n_h
         ROCKET_LOGE("%s: head_dim %d unsupported (the fused kernel is built for 64)\n", who, d / n_head);
         return ROCKET_E_UNSUPPORTED;
     }
-    enc_call c;
-    int rc = enc_begin(&c, fd, who);
+    rkb_call c;
+    int rc = rkb_call_begin(&c, fd, who);
     if (rc) return rc;
     const int BT = nb * T;
     const size_t act = (size_t)BT * d * 2, w = (size_t)d * d * 2, v = (size_t)d * 2;
-    const void *dx = enc_in(&c, x, act);
-    const void *g1 = enc_in(&c, ln1_g, v), *b1 = enc_in(&c, ln1_b, v);
-    const void *g2 = enc_in(&c, ln2_g, v), *b2 = enc_in(&c, ln2_b, v);
-    const void *dq = enc_in(&c, Wq, w), *dk = enc_in(&c, Wk, w), *dv = enc_in(&c, Wv, w), *dwo = enc_in(&c, Wo, w);
-    const void *dbq = enc_in(&c, bq, v), *dbk = enc_in(&c, bk, v), *dbv = enc_in(&c, bv, v), *dbo = enc_in(&c, bo, v);
-    const void *dw1 = enc_in(&c, Wf1, (size_t)d_ff * d * 2), *dbf1 = enc_in(&c, bf1, (size_t)d_ff * 2);
-    const void *dw2 = enc_in(&c, Wf2, (size_t)d * d_ff * 2), *dbf2 = enc_in(&c, bf2, v);
-    void *ln = enc_tmp(&c, act), *ctx = enc_tmp(&c, act), *xa = enc_tmp(&c, act);
-    void *f1 = enc_tmp(&c, (size_t)BT * d_ff * 2);
-    void *dout = enc_out(&c, out, act);
+    const void *dx = rkb_call_in(&c, x, act);
+    const void *g1 = rkb_call_in(&c, ln1_g, v), *b1 = rkb_call_in(&c, ln1_b, v);
+    const void *g2 = rkb_call_in(&c, ln2_g, v), *b2 = rkb_call_in(&c, ln2_b, v);
+    const void *dq = rkb_call_in(&c, Wq, w), *dk = rkb_call_in(&c, Wk, w), *dv = rkb_call_in(&c, Wv, w), *dwo = rkb_call_in(&c, Wo, w);
+    const void *dbq = rkb_call_in(&c, bq, v), *dbk = rkb_call_in(&c, bk, v), *dbv = rkb_call_in(&c, bv, v), *dbo = rkb_call_in(&c, bo, v);
+    const void *dw1 = rkb_call_in(&c, Wf1, (size_t)d_ff * d * 2), *dbf1 = rkb_call_in(&c, bf1, (size_t)d_ff * 2);
+    const void *dw2 = rkb_call_in(&c, Wf2, (size_t)d * d_ff * 2), *dbf2 = rkb_call_in(&c, bf2, v);
+    void *ln = rkb_call_tmp(&c, act), *ctx = rkb_call_tmp(&c, act), *xa = rkb_call_tmp(&c, act);
+    void *f1 = rkb_call_tmp(&c, (size_t)BT * d_ff * 2);
+    void *dout = rkb_call_out(&c, out, act);
     if (!c.rc) {
         int ps = rkb_prof_begin(c.h);
-        enc_check(&c, rkb_norm_rows(dx, g1, b1, BT, d, eps, 0, ln, c.h->stream));
+        rkb_call_check(&c, rkb_norm_rows(dx, g1, b1, BT, d, eps, 0, ln, c.h->stream));
         rkb_prof_end(c.h, ps, RKB_K_NORM);
     }
     enc_mha_core(&c, nb, T, d, n_head, ln, dq, dbq, dk, dbk, dv, dbv, ctx);
-    enc_gemm(&c, BT, d, d, ctx, d, dwo, xa, d, dbo, RKB_ACT_NONE, dx, d);          /* x + MHA */
+    rkb_call_gemm(&c, BT, d, d, ctx, d, dwo, xa, d, dbo, RKB_ACT_NONE, dx, d);          /* x + MHA */
     if (!c.rc) {
         int ps = rkb_prof_begin(c.h);
-        enc_check(&c, rkb_norm_rows(xa, g2, b2, BT, d, eps, 0, ln, c.h->stream));
+        rkb_call_check(&c, rkb_norm_rows(xa, g2, b2, BT, d, eps, 0, ln, c.h->stream));
         rkb_prof_end(c.h, ps, RKB_K_NORM);
     }
-    enc_gemm(&c, BT, d_ff, d, ln, d, dw1, f1, d_ff, dbf1, RKB_ACT_GELU, NULL, 0);  /* GELU(fc1) */
-    enc_gemm(&c, BT, d, d_ff, f1, d_ff, dw2, dout, d, dbf2, RKB_ACT_NONE, xa, d);  /* + residual */
+    rkb_call_gemm(&c, BT, d_ff, d, ln, d, dw1, f1, d_ff, dbf1, RKB_ACT_GELU, NULL, 0);  /* GELU(fc1) */
+    rkb_call_gemm(&c, BT, d, d_ff, f1, d_ff, dw2, dout, d, dbf2, RKB_ACT_NONE, xa, d);  /* + residual */
     rkb_count(0, 2);
-    return enc_end(&c);
+    return rkb_call_end(&c);
 }
 
 int rocket_encoder_block_fp16(int fd, int T, int d, int n_head, int d_ff, const _Float16 *x,
@@ -455,4 +342,58 @@ int rocket_b200_encoder_block_batched_fp16(int fd, int nb, int T, int d, int n_h
     return encoder_common("rocket_b200_encoder_block_batched_fp16", fd, nb, T, d, n_head, d_ff, x,
                           ln1_g, ln1_b, Wq, bq, Wk, bk, Wv, bv, Wo, bo, ln2_g, ln2_b, Wf1, bf1, Wf2,
                           bf2, eps, out);
+}
+
+/* ---- reductions ---------------------------------------------------------------------------
+ * Reference: src/rocket_reduce.c:380-510 (feature reduce, cumsum via ones / triangular
+ * matmuls), src/rocket_norm.c:21-60 (scale_rows), src/rocket_softmax.c:141-190 (cross
+ * entropy).  Each is one warp-per-row (or element-wise) pass in fp32. */
+int rocket_reduce_feature_fp16(int fd, int M, int H, const _Float16 *in, float *out, int mean)
+{
+    if (M < 1 || H < 1 || !in || !out) return ROCKET_E_SHAPE;
+    rkb_call c;
+    int rc = rkb_call_begin(&c, fd, "rocket_reduce_feature_fp16");
+    if (rc) return rc;
+    const void *dx = rkb_call_in(&c, in, (size_t)M * H * 2);
+    float *dout = rkb_call_out(&c, out, (size_t)M * 4);
+    if (!c.rc) rkb_call_check(&c, rkb_reduce_rows(dx, M, H, mean, dout, c.h->stream));
+    return rkb_call_end(&c);
+}
+
+int rocket_cumsum_fp16(int fd, int M, int N, const _Float16 *in, _Float16 *out, int exclusive, int reverse)
+{
+    if (M < 1 || N < 1 || !in || !out) return ROCKET_E_SHAPE;
+    rkb_call c;
+    int rc = rkb_call_begin(&c, fd, "rocket_cumsum_fp16");
+    if (rc) return rc;
+    const void *dx = rkb_call_in(&c, in, (size_t)M * N * 2);
+    void *dout = rkb_call_out(&c, out, (size_t)M * N * 2);
+    if (!c.rc) rkb_call_check(&c, rkb_cumsum_rows(dx, M, N, exclusive, reverse, dout, c.h->stream));
+    return rkb_call_end(&c);
+}
+
+int rocket_scale_rows_fp16(int fd, int M, int N, const _Float16 *in, const float *r, _Float16 *out)
+{
+    if (M < 1 || N < 1 || !in || !r || !out) return ROCKET_E_SHAPE;
+    rkb_call c;
+    int rc = rkb_call_begin(&c, fd, "rocket_scale_rows_fp16");
+    if (rc) return rc;
+    const void *dx = rkb_call_in(&c, in, (size_t)M * N * 2);
+    const float *dr = rkb_call_in(&c, r, (size_t)M * 4);
+    void *dout = rkb_call_out(&c, out, (size_t)M * N * 2);
+    if (!c.rc) rkb_call_check(&c, rkb_scale_rows(dx, dr, M, N, dout, c.h->stream));
+    return rkb_call_end(&c);
+}
+
+int rocket_cross_entropy_fp16(int fd, int M, int N, const _Float16 *logits, const int *target, float *loss)
+{
+    if (M < 1 || N < 1 || !logits || !target || !loss) return ROCKET_E_SHAPE;
+    rkb_call c;
+    int rc = rkb_call_begin(&c, fd, "rocket_cross_entropy_fp16");
+    if (rc) return rc;
+    const void *dx = rkb_call_in(&c, logits, (size_t)M * N * 2);
+    const int *dt = rkb_call_in(&c, target, (size_t)M * 4);
+    float *dl = rkb_call_out(&c, loss, (size_t)M * 4);
+    if (!c.rc) rkb_call_check(&c, rkb_cross_entropy_rows(dx, dt, M, N, dl, c.h->stream));
+    return rkb_call_end(&c);
 }

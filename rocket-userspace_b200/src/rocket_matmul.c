@@ -124,8 +124,8 @@ int rkb_gw_on(rkb_handle *h, int M, int N, int K, int group, int w_bits,
 }
 
 /* ---- one-shot entries ---------------------------------------------------- */
-static int oneshot_dense(const char *who, int fd, int in_kind, int out_kind, int M, int K, int N,
-                         const void *A, const void *B, void *C)
+int rkb_oneshot_dense(const char *who, int fd, int in_kind, int out_kind, int M, int K, int N,
+                      const void *A, const void *B, void *C, int finish)
 {
     rkb_handle *h = rkb_get(fd);
     if (!h) {
@@ -133,7 +133,7 @@ static int oneshot_dense(const char *who, int fd, int in_kind, int out_kind, int
         return ROCKET_E_DEVICE;
     }
     if (!A || !B || !C) return ROCKET_E_SHAPE;
-    const size_t esz = in_kind == RKB_IN_F16 ? 2 : 1;
+    const size_t esz = in_kind == RKB_IN_I8 ? 1 : in_kind == RKB_IN_TF32 ? 4 : 2;
     const size_t osz = out_kind == RKB_OUT_F16 ? 2 : 4;
     const void *dA = rkb_stage_in(h, RKB_SCR_A, A, (size_t)M * K * esz);
     const void *dB = rkb_stage_in(h, RKB_SCR_B, B, (size_t)N * K * esz);
@@ -143,9 +143,16 @@ static int oneshot_dense(const char *who, int fd, int in_kind, int out_kind, int
     int rc = rkb_dense_on(h, in_kind, out_kind, M, N, K, dA, K, dB, K, dC, N);
     if (!rc) rc = rkb_stage_out_finish(h, C, dC, (size_t)M * N * osz, cb);
     rkb_count(1, 0);
+    if (!finish && !rc) return 0;   /* caller waits once for a batch of calls */
     if (!rc && rkb_async_enabled() && dA == A && dB == B && !cb) return 0;   /* deferred */
     int fr = rkb_finish(h, who);
     return rc ? rc : fr;
+}
+
+static int oneshot_dense(const char *who, int fd, int in_kind, int out_kind, int M, int K, int N,
+                         const void *A, const void *B, void *C)
+{
+    return rkb_oneshot_dense(who, fd, in_kind, out_kind, M, K, N, A, B, C, 1);
 }
 
 int rocket_matmul_fp16(int fd, int M, int K, int N, const _Float16 *A, const _Float16 *B,

@@ -28,7 +28,7 @@
 #include "rocket_b200.h"
 #include "rkb_internal.h"
 
-typedef enum { RW_F16, RW_I8, RW_I8_GW, RW_I4, RW_I4_GW } rw_kind;
+typedef enum { RW_F16, RW_I8, RW_I8_GW, RW_I4, RW_I4_GW, RW_BF16 } rw_kind;
 
 typedef struct {
     int nthreads;
@@ -42,6 +42,7 @@ typedef struct {
     int n0[RKB_MAX_WORKERS], nsub[RKB_MAX_WORKERS];
     void *dev[RKB_MAX_WORKERS];
     size_t bytes[RKB_MAX_WORKERS];
+    size_t cap[RKB_MAX_WORKERS];
 } rkb_rweights;
 
 struct rocket_ctx        { rkb_rctx r; };
@@ -107,15 +108,28 @@ static int nstep(int N, int nthreads, int atom)
 }
 
 /* ---- weights ---------------------------------------------------------------- */
-static int rweights_pack(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M, int K, int N,
-                         const void *B, int group, const char *who)
+/* Fill w with the workers' N-slices of the weight.  The weight is given as nseg
+ * row blocks Bs[i] of Ns[i] rows each (one block for a plain weight; several
+ * for a fused N-concatenation).  Existing per-worker buffers large enough are
+ * reused (the streaming contexts re-fill every call); finish = 0 leaves the
+ * copies queued for the call that follows. */
+static int rweights_fill(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M, int K, int N, int nseg,
+                         const void *const *Bs, const int *Ns, int group, int finish, const char *who)
 {
+    void *keep[RKB_MAX_WORKERS];
+    size_t keep_cap[RKB_MAX_WORKERS];
+    memcpy(keep, w->dev, sizeof keep);
+    memcpy(keep_cap, w->cap, sizeof keep_cap);
     memset(w, 0, sizeof *w);
+    memcpy(w->dev, keep, sizeof keep);
+    memcpy(w->cap, keep_cap, sizeof keep_cap);
     w->kind = kind; w->M = M; w->K = K; w->N = N; w->group = group;
     const int step = nstep(N, c->nthreads, c->atom);
-    const size_t esz = kind == RW_F16 ? 2 : 1;
+    const size_t esz = kind == RW_F16 ? 2 : kind == RW_BF16 ? 4 : 1;   /* caller's element size */
+    const int gw = (kind == RW_I8_GW || kind == RW_I4_GW || kind == RW_I4);
+    if (gw && nseg != 1) return ROCKET_E_SHAPE;
     int rc = 0;
-    for (int t = 0; t < c->nthreads; t++) {
+    for (int t = 0; t < c->nthreads && !rc; t++) {
         const int n0 = t * step;
         const int nsub = n0 >= N ? 0 : (N - n0 < step ? N - n0 : step);
         w->n0[t] = n0;
@@ -123,36 +137,69 @@ static int rweights_pack(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M
         if (nsub <= 0) continue;
         w->nt = t + 1;
         rkb_handle *h = rkb_get(c->fd[t]);
-        const void *src = (const uint8_t *)B + (size_t)n0 * K * esz;
         const size_t raw = (size_t)nsub * K * esz;
-        if (kind == RW_F16 || kind == RW_I8) {
-            w->bytes[t] = raw;
-            if (cudaMalloc(&w->dev[t], raw) != cudaSuccess) { rc = ROCKET_E_NOMEM; break; }
-            if (cudaMemcpyAsync(w->dev[t], src, raw, cudaMemcpyDefault, h->stream) != cudaSuccess) {
-                rc = ROCKET_E_DEVICE;
-                break;
-            }
-        } else {
-            const int bits = (kind == RW_I8_GW) ? 8 : 4;
-            w->bytes[t] = rkb_wpack_codes_bytes(nsub, K, bits);
+        size_t need;
+        if (gw) need = rkb_wpack_codes_bytes(nsub, K, kind == RW_I8_GW ? 8 : 4);
+        else if (kind == RW_BF16) need = (size_t)nsub * K * 2;
+        else need = raw;
+        w->bytes[t] = need;
+        if (w->cap[t] < need) {
+            if (w->dev[t]) { cudaStreamSynchronize(h->stream); cudaFree(w->dev[t]); }
+            w->dev[t] = NULL;
+            w->cap[t] = 0;
+            if (cudaMalloc(&w->dev[t], need) != cudaSuccess) { cudaGetLastError(); rc = ROCKET_E_NOMEM; break; }
+            w->cap[t] = need;
+        }
+        if (gw) {
+            const void *src = (const uint8_t *)Bs[0] + (size_t)n0 * K;
             const void *dsrc = rkb_stage_in(h, RKB_SCR_B, src, raw);
-            if (!dsrc || cudaMalloc(&w->dev[t], w->bytes[t]) != cudaSuccess) { rc = ROCKET_E_NOMEM; break; }
+            if (!dsrc) { rc = ROCKET_E_NOMEM; break; }
             int ps = rkb_prof_begin(h);
-            rc = rkb_wpack_codes(dsrc, nsub, K, bits, w->dev[t], h->stream);
+            rc = rkb_wpack_codes(dsrc, nsub, K, kind == RW_I8_GW ? 8 : 4, w->dev[t], h->stream);
             rkb_prof_end(h, ps, RKB_K_PACK);
-            if (rc) break;
+        } else {
+            /* gather the slice rows [n0, n0+nsub) from the segments */
+            uint8_t *dst = w->dev[t];
+            if (kind == RW_BF16) dst = rkb_scratch(h, RKB_SCR_B, raw);   /* fp32 staging */
+            if (!dst) { rc = ROCKET_E_NOMEM; break; }
+            int base = 0;
+            for (int sg = 0; sg < nseg && !rc; sg++) {
+                const int lo = n0 > base ? n0 : base;
+                const int hi = (n0 + nsub) < (base + Ns[sg]) ? (n0 + nsub) : (base + Ns[sg]);
+                if (hi > lo) {
+                    const uint8_t *src = (const uint8_t *)Bs[sg] + (size_t)(lo - base) * K * esz;
+                    if (cudaMemcpyAsync(dst + (size_t)(lo - n0) * K * esz, src, (size_t)(hi - lo) * K * esz,
+                                        cudaMemcpyDefault, h->stream) != cudaSuccess) {
+                        cudaGetLastError();
+                        rc = ROCKET_E_DEVICE;
+                    }
+                }
+                base += Ns[sg];
+            }
+            if (!rc && kind == RW_BF16) rc = rkb_f32_to_bf16(dst, (size_t)nsub * K, w->dev[t], h->stream);
         }
         rkb_count(1, 1);
     }
-    for (int t = 0; t < w->nt; t++) {
-        int fr = rkb_finish(rkb_get(c->fd[t]), who);
-        if (!rc) rc = fr;
+    if (finish || rc) {
+        for (int t = 0; t < w->nt; t++) {
+            int fr = rkb_finish(rkb_get(c->fd[t]), who);
+            if (!rc) rc = fr;
+        }
     }
+    if (rc) ROCKET_LOGE("%s: weight upload failed (%d)\n", who, rc);
+    return rc;
+}
+
+static int rweights_pack(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M, int K, int N,
+                         const void *B, int group, const char *who)
+{
+    memset(w, 0, sizeof *w);
+    const void *bs[1] = {B};
+    const int ns[1] = {N};
+    int rc = rweights_fill(c, w, kind, M, K, N, 1, bs, ns, group, 1, who);
     if (rc) {
-        cudaGetLastError();
         for (int t = 0; t < c->nthreads; t++)
-            if (w->dev[t]) { cudaSetDevice(rkb_get(c->fd[t])->device); cudaFree(w->dev[t]); }
-        ROCKET_LOGE("%s: pack failed (%d)\n", who, rc);
+            if (w->dev[t]) { rkb_get(c->fd[t]); cudaFree(w->dev[t]); w->dev[t] = NULL; }
     }
     return rc;
 }
@@ -165,6 +212,7 @@ static void rweights_free(const rkb_rctx *c, rkb_rweights *w)
         if (h) cudaStreamSynchronize(h->stream);
         cudaFree(w->dev[t]);
         w->dev[t] = NULL;
+        w->cap[t] = 0;
     }
 }
 
@@ -187,7 +235,7 @@ static int rrun(const rkb_rctx *c, const rkb_rweights *w, int M, const rrun_args
                 const char *who)
 {
     const int K = w->K, N = w->N;
-    const size_t esz = w->kind == RW_F16 ? 2 : 1;
+    const size_t esz = w->kind == RW_F16 ? 2 : w->kind == RW_BF16 ? 4 : 1;
     const size_t osz = a->out_kind == RKB_OUT_F16 ? 2 : 4;
     const int c_dev = rkb_ptr_device(a->C);
     int rows_const = 0;
@@ -216,6 +264,12 @@ static int rrun(const rkb_rctx *c, const rkb_rweights *w, int M, const rrun_args
         case RW_I8:
             rc = rkb_dense_on(h, RKB_IN_I8, RKB_OUT_I32, M, nsub, K, dA, K, w->dev[t], K, dC, ldc);
             break;
+        case RW_BF16: {
+            void *a16 = rkb_scratch(h, RKB_SCR_AUX, (size_t)M * K * 2);
+            rc = a16 ? rkb_f32_to_bf16(dA, (size_t)M * K, a16, h->stream) : ROCKET_E_NOMEM;
+            if (!rc) rc = rkb_dense_on(h, RKB_IN_BF16, RKB_OUT_F32, M, nsub, K, a16, K, w->dev[t], K, dC, ldc);
+            break;
+        }
         case RW_I4: {
             rkb_wgemm_desc d;
             memset(&d, 0, sizeof d);
@@ -523,4 +577,92 @@ int rocket_matmul_int4_prepacked_gw(rocket_i4_ctx *ctx, int M, int K, int N, con
     if (rc) return rc;
     rrun_args a = { A, Cf, a_scale, b_scale, RKB_OUT_F32 };
     return rrun(&ctx->r, &w->w, M, &a, "rocket_matmul_int4_prepacked_gw");
+}
+
+/* ---- streaming contexts: weights re-uploaded every call ----------------------
+ * Reference: src/rocket_prepacked.c:459-505 (rocket_stream / _fused) and
+ * src/rocket_bf16_stream.c:344-549 (bf16 mt / stream).  A stream keeps its
+ * workers and their weight buffers across calls and re-fills them with each
+ * call's B (or the N-concatenation of several Bs), so an LLM's repeating shape
+ * set pays device allocation once. */
+struct rocket_stream      { rkb_rctx r; rkb_rweights w; };
+struct rocket_bf16_stream { rkb_rctx r; rkb_rweights w; };
+
+rocket_stream *rocket_stream_create(int nthreads)
+{
+    rocket_stream *s = calloc(1, sizeof *s);
+    if (!s) return NULL;
+    if (rctx_init(&s->r, nthreads, 16, "rocket_stream_create")) { free(s); return NULL; }
+    return s;
+}
+
+void rocket_stream_free(rocket_stream *s)
+{
+    if (!s) return;
+    rweights_free(&s->r, &s->w);
+    rctx_free(&s->r);
+    free(s);
+}
+
+int rocket_matmul_fp16_stream_fused(rocket_stream *s, int M, int K, const _Float16 *const *Bs,
+                                    const int *Ns, int nseg, const _Float16 *A, _Float16 *C)
+{
+    const char *who = "rocket_matmul_fp16_stream_fused";
+    if (!s || !Bs || !Ns || !A || !C || nseg < 1 || nseg > ROCKET_MAX_FUSE) return ROCKET_E_SHAPE;
+    int N = 0;
+    for (int i = 0; i < nseg; i++) {
+        if (!Bs[i] || Ns[i] <= 0) return ROCKET_E_SHAPE;
+        N += Ns[i];
+    }
+    if (rocket_matmul_plan(M, K, N, NULL, NULL, NULL) < 0 || M % 4) return ROCKET_E_SHAPE;
+    int rc = rweights_fill(&s->r, &s->w, RW_F16, M, K, N, nseg, (const void *const *)Bs, Ns, 0, 0, who);
+    if (rc) return rc;
+    rrun_args a = { A, C, NULL, NULL, RKB_OUT_F16 };
+    return rrun(&s->r, &s->w, M, &a, who);
+}
+
+int rocket_matmul_fp16_stream(rocket_stream *s, int M, int K, int N, const _Float16 *A,
+                              const _Float16 *B, _Float16 *C)
+{
+    const _Float16 *bs[1] = {B};
+    const int ns[1] = {N};
+    return rocket_matmul_fp16_stream_fused(s, M, K, bs, ns, 1, A, C);
+}
+
+rocket_bf16_stream *rocket_bf16_stream_create(int nthreads)
+{
+    rocket_bf16_stream *s = calloc(1, sizeof *s);
+    if (!s) return NULL;
+    if (rctx_init(&s->r, nthreads, 16, "rocket_bf16_stream_create")) { free(s); return NULL; }
+    return s;
+}
+
+void rocket_bf16_stream_free(rocket_bf16_stream *s)
+{
+    if (!s) return;
+    rweights_free(&s->r, &s->w);
+    rctx_free(&s->r);
+    free(s);
+}
+
+int rocket_matmul_bf16_stream(rocket_bf16_stream *s, int M, int K, int N, const float *A,
+                              const float *B, float *C)
+{
+    const char *who = "rocket_matmul_bf16_stream";
+    if (!s || !A || !B || !C || rocket_matmul_plan(M, K, N, NULL, NULL, NULL) < 0) return ROCKET_E_SHAPE;
+    const void *bs[1] = {B};
+    const int ns[1] = {N};
+    int rc = rweights_fill(&s->r, &s->w, RW_BF16, M, K, N, 1, bs, ns, 0, 0, who);
+    if (rc) return rc;
+    rrun_args a = { A, C, NULL, NULL, RKB_OUT_F32 };
+    return rrun(&s->r, &s->w, M, &a, who);
+}
+
+int rocket_matmul_bf16_mt(int M, int K, int N, const float *A, const float *B, float *C, int nthreads)
+{
+    rocket_bf16_stream *s = rocket_bf16_stream_create(nthreads);
+    if (!s) return ROCKET_E_DEVICE;
+    int rc = rocket_matmul_bf16_stream(s, M, K, N, A, B, C);
+    rocket_bf16_stream_free(s);
+    return rc;
 }

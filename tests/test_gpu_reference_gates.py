@@ -25,6 +25,19 @@ CASES = [
     ("matmul_int8_prepacked_rocket", []),
     ("matmul_int4_prepacked_rocket", []),
     ("matmul_mt_rocket", ["512", "3840", "4096"]),
+    # widened entries: dtypes, batch, streaming, reductions
+    ("matmul_bf16_tiled_rocket", ["512", "3840", "4096"]),
+    ("matmul_bf16_tiled_rocket", ["1", "512", "256"]),
+    ("matmul_tf32_tiled_rocket", ["512", "3840", "4096"]),
+    ("matmul_tf32_tiled_rocket", ["68", "272", "144"]),
+    ("matmul_int16_exact_rocket", ["256", "1024", "512"]),
+    ("matmul_int16_exact_rocket", ["1", "64", "32"]),
+    ("matmul_batch_rocket", []),
+    ("matmul_bf16_stream_rocket", ["512", "3840", "4096", "4"]),
+    ("matmul_stream_vs_prepacked_rocket", ["1024", "3840", "4096", "5", "5"]),
+    ("cumsum_rocket", []),
+    ("cross_entropy_rocket", []),
+    ("reduce_feature_rocket", []),
 ]
 
 
