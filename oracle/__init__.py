@@ -327,3 +327,47 @@ def reduce_golden_inputs():
     t = (np.arange(33, dtype=np.int64) * 397 % 1000).astype(np.int32)
     t[5], t[11] = -1, 1000
     return {"x": x, "r": r, "logits": logits, "target": t}
+
+
+# ---- masked grouped-query attention ----
+lib.orc_flash_attn_f16.restype = None
+lib.orc_flash_attn_f16.argtypes = [ctypes.c_int] * 6 + [ctypes.c_float] * 2 + [ctypes.c_void_p] * 5
+
+
+def flash_attn(Q, K, V, mask, scale, softcap=0.0):
+    """Q [nh, T, dh], K [nkvh, n_kv, dh], V [nkvh, dv, n_kv], mask [T, n_kv] or None."""
+    nh, T, dh = Q.shape
+    nkvh, n_kv, _ = K.shape
+    dv = V.shape[1]
+    out = np.empty((nh, T, dv), np.float16)
+    lib.orc_flash_attn_f16(T, n_kv, dh, dv, nh, nkvh, scale, softcap, _h(Q), _h(K), _h(V), _h(mask),
+                           out.ctypes.data)
+    return out
+
+
+def causal_mask(T, n_kv, window=0):
+    """Additive causal (+ sliding window) mask [T, n_kv] with keys aligned to the
+    tail of the cache (tests/flash_attn_rocket.c:44-52 convention): 0 kept, -inf masked."""
+    pos = n_kv - T + np.arange(T)[:, None]
+    j = np.arange(n_kv)[None, :]
+    keep = (j <= pos) & ((window <= 0) | (j > pos - window))
+    return np.where(keep, 0.0, -np.inf).astype(np.float16)
+
+
+# (T, n_kv, dh, dv, nh, nkvh, window, softcap): the reference gate's cases, scaled down
+FA_GOLDEN_CASES = [
+    (32, 32, 64, 64, 4, 2, 0, 0.0),
+    (20, 45, 96, 96, 4, 1, 8, 0.0),
+    (16, 64, 192, 128, 2, 1, 0, 0.0),
+    (24, 24, 128, 128, 2, 2, 0, 50.0),
+    (8, 40, 256, 256, 2, 1, 0, 0.0),
+]
+
+
+def fa_golden_inputs(case):
+    T, n_kv, dh, dv, nh, nkvh, window, _ = case
+    seed = T * 1000 + n_kv * 10 + dh
+    Q = normal_f16(seed + 1, 1.0, (nh, T, dh))
+    K = normal_f16(seed + 2, 1.0, (nkvh, n_kv, dh))
+    V = normal_f16(seed + 3, 1.0, (nkvh, dv, n_kv))
+    return Q, K, V, causal_mask(T, n_kv, window)

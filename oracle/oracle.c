@@ -469,3 +469,68 @@ void orc_cross_entropy_f16(int M, int N, const uint16_t *x, const int *target, f
         loss[m] = (float)(mx + log(s) - g);
     }
 }
+
+/* src/rocket_attn.c:181-187 (fa_score) and :189-222 (masked GQA attention host loop):
+ * fp64 dot products, the score transform in float, fp64 softmax and P.V */
+static float fa_score_ref(float qk, float scale, float softcap, float m)
+{
+    float s = qk * scale;
+    if (softcap != 0.0f) s = softcap * tanhf(s / softcap);
+    s += m;
+    return s < -30000.0f ? -30000.0f : s;
+}
+
+typedef struct {
+    int T, n_kv, dh, dv, nh, nkvh;
+    float scale, softcap;
+    const uint16_t *Q, *K, *V, *mask;
+    uint16_t *out;
+} fa_args;
+
+/* rows r = h * T + t, each computed independently */
+static void fa_rows(void *p, int r0, int r1)
+{
+    const fa_args *a = p;
+    const int T = a->T, n_kv = a->n_kv, dh = a->dh, dv = a->dv, gqa = a->nh / a->nkvh;
+    double *sc = malloc((size_t)n_kv * sizeof(double));
+    if (!sc) return;
+    for (int r = r0; r < r1; r++) {
+        const int h = r / T, t = r % T, hk = h / gqa;
+        const uint16_t *qr = a->Q + ((size_t)h * T + t) * dh;
+        const uint16_t *Kh = a->K + (size_t)hk * n_kv * dh;
+        const uint16_t *Vh = a->V + (size_t)hk * dv * n_kv;
+        uint16_t *orow = a->out + ((size_t)h * T + t) * dv;
+        double mx = -INFINITY;
+        for (int j = 0; j < n_kv; j++) {
+            double qk = 0;
+            for (int c = 0; c < dh; c++) qk += hd(qr[c]) * hd(Kh[(size_t)j * dh + c]);
+            const float mj = a->mask ? orc_h2f(a->mask[(size_t)t * n_kv + j]) : 0.0f;
+            sc[j] = fa_score_ref((float)qk, a->scale, a->softcap, mj);
+            if (sc[j] > mx) mx = sc[j];
+        }
+        double sum = 0;
+        for (int j = 0; j < n_kv; j++) { sc[j] = exp(sc[j] - mx); sum += sc[j]; }
+        const double inv = sum > 0 ? 1.0 / sum : 0.0;
+        for (int c = 0; c < dv; c++) {
+            double acc = 0;
+            for (int j = 0; j < n_kv; j++) acc += sc[j] * hd(Vh[(size_t)c * n_kv + j]);
+            orow[c] = dh16(acc * inv);
+        }
+    }
+    free(sc);
+}
+
+void orc_flash_attn_f16_mt(int T, int n_kv, int dh, int dv, int nh, int nkvh, float scale, float softcap,
+                           const uint16_t *Q, const uint16_t *K, const uint16_t *V, const uint16_t *mask,
+                           uint16_t *out, int nthreads)
+{
+    fa_args a = {T, n_kv, dh, dv, nh, nkvh, scale, softcap, Q, K, V, mask, out};
+    run_rows(fa_rows, &a, 0, nh * T, nthreads);
+}
+
+void orc_flash_attn_f16(int T, int n_kv, int dh, int dv, int nh, int nkvh, float scale, float softcap,
+                        const uint16_t *Q, const uint16_t *K, const uint16_t *V, const uint16_t *mask,
+                        uint16_t *out)
+{
+    orc_flash_attn_f16_mt(T, n_kv, dh, dv, nh, nkvh, scale, softcap, Q, K, V, mask, out, 1);
+}

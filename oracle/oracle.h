@@ -62,6 +62,14 @@ void orc_cumsum_f16(int M, int N, const uint16_t *x, int exclusive, int reverse,
 void orc_scale_rows_f16(int M, int N, const uint16_t *x, const float *r, uint16_t *y);
 void orc_cross_entropy_f16(int M, int N, const uint16_t *x, const int *target, float *loss);
 
+/* masked grouped-query attention */
+void orc_flash_attn_f16(int T, int n_kv, int dh, int dv, int nh, int nkvh, float scale, float softcap,
+                        const uint16_t *Q, const uint16_t *K, const uint16_t *V, const uint16_t *mask,
+                        uint16_t *out);
+void orc_flash_attn_f16_mt(int T, int n_kv, int dh, int dv, int nh, int nkvh, float scale, float softcap,
+                           const uint16_t *Q, const uint16_t *K, const uint16_t *V, const uint16_t *mask,
+                           uint16_t *out, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -157,6 +157,11 @@ _SIGS += [
     ("rocket_stream_free", None, [_P]),
     ("rocket_matmul_fp16_stream", c_int, [_P, c_int, c_int, c_int, _P, _P, _P]),
     ("rocket_matmul_fp16_stream_fused", c_int, [_P, c_int, c_int, _P, _P, c_int, _P, _P]),
+    ("rocket_fa_ctx_create", _P, [c_int]),
+    ("rocket_fa_ctx_free", None, [_P]),
+    ("rocket_flash_attn_fp16", c_int, [c_int] * 7 + [c_float, c_float] + [_P] * 5),
+    ("rocket_flash_attn_fp16_mt", c_int, [c_int] * 7 + [c_float, c_float] + [_P] * 5 + [c_int]),
+    ("rocket_flash_attn_fp16_ctx", c_int, [_P] + [c_int] * 6 + [c_float, c_float] + [_P] * 5),
 ]
 
 ENCODER_KEYS = ["ln1_g", "ln1_b", "Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo", "ln2_g", "ln2_b",

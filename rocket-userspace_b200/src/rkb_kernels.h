@@ -101,6 +101,11 @@ int rkb_elementwise(const void *a, const void *b, int op, int kind, size_t n, vo
 int rkb_split_heads(const void *qkv, long ld, int B, int T, int Tp, int H, int dh, void *Q,
                     void *K, void *Vt, cudaStream_t s);
 /* out[b*T + t, h*dh + c] = softmax(Q K^T * scale) V per (b, h); dh == 64, Tp % 128 == 0 */
+/* masked GQA flash attention (csrc/fa_tc.cu): Q [nh][T][dh], K [nkvh][n_kv][dh],
+ * V [nkvh][dv] rows of ldv elements, mask [T][n_kv] or NULL, out [nh][T][dv] */
+int rkb_flash_attn(const void *Q, const void *K, const void *V, long ldv, const void *mask, void *out,
+                   int T, int n_kv, int dh, int dv, int n_head, int n_kv_heads, float scale,
+                   float softcap, int *err, cudaStream_t stream);
 int rkb_attention(const void *Q, const void *K, const void *Vt, int B, int H, int T, int Tp,
                   int dh, float scale, void *out, long ldo, int *err, cudaStream_t stream);
 

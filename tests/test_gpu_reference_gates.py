@@ -38,6 +38,10 @@ CASES = [
     ("cumsum_rocket", []),
     ("cross_entropy_rocket", []),
     ("reduce_feature_rocket", []),
+    ("matmul_fp32out_rocket", ["64", "4096", "512"]),
+    ("matmul_fp32out_rocket", ["1", "64", "48"]),
+    ("flash_attn_rocket", []),                              # full sweep: GQA/MQA/MLA/window/softcap/long
+    ("flash_attn_rocket", ["256", "1024", "128", "8", "2"]),
 ]
 
 
