@@ -242,8 +242,10 @@ def main_ours(args):
     clocks = Clocks(local)
     clocks.start()
     time.sleep(0.3)
-    L.rocket_b200_profile_reset()
-    L.rocket_b200_profile_enable(1)
+    # the timed region runs without the per-kernel profiler: its CUDA events
+    # between kernels cost device time; kernel durations come from a separate
+    # profiled pass below
+    L.rocket_b200_profile_enable(0)
     L.rocket_submit_counters_reset()
     barrier()
     torch.cuda.synchronize()
@@ -263,10 +265,24 @@ def main_ours(args):
     assert rc_sync == 0, f"ctx_sync {rc_sync}"
     torch.cuda.synchronize()
     barrier()
-    L.rocket_b200_profile_enable(0)
     launches = int(L.rocket_submit_task_count())
     clk = clocks.stop()
     ms = e0.elapsed_time(e1)
+    # profiled pass: per-kernel CUDA events on the library stream
+    prof_steps = max(1, min(args.steps, 50))
+    L.rocket_b200_profile_reset()
+    L.rocket_b200_profile_enable(1)
+    L.rocket_b200_set_async(1)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(lib_stream)
+    for _ in range(prof_steps):
+        step()
+    p1.record(lib_stream)
+    assert L.rocket_b200_ctx_sync(ctx) == 0
+    L.rocket_b200_set_async(0)
+    torch.cuda.synchronize()
+    L.rocket_b200_profile_enable(0)
+    prof_ms = p0.elapsed_time(p1)
     ms_max = max_over_ranks(ms)
     step_ops = SET_OPS if not args.layers else sum(
         2.0 * M_TOK * k * n for nm, k, n in GEMMS if nm in args.layers.split(","))
@@ -289,7 +305,8 @@ def main_ours(args):
                 "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
                 "kernel": "gemm_i8_tcgen05", "launches": n_i8,
                 "avg_launch_us": avg_launch_ms * 1e3,
-                "kernel_share_of_step": ms_i8 / ms if ms > 0 else None}
+                "profiled_pass": f"{prof_steps} steps with per-kernel events, apart from the timed region",
+                "kernel_share_of_step": ms_i8 / prof_ms if prof_ms > 0 else None}
     traffic_file = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(traffic_file):
         roofline["traffic"] = json.load(open(traffic_file)).get("gemm_i8_config5_avg_launch_bytes")

@@ -85,6 +85,15 @@ int rocket_b200_encoder_block_batched_fp16(int fd, int nb, int T, int d, int n_h
                                            const void *Wf2, const void *bf2,
                                            float eps, void *out);
 
+/* Dense GEMM kernel policy for this process (default: automatic).
+ *   variant   0 automatic; 128 / 256 single-CTA tiles 128 x 128 / 128 x 256;
+ *             384 / 512 CTA-pair tiles 256 x 128 / 256 x 256
+ *   stream_k  -1 automatic; 0 never; 1 whenever the pair tiling leaves the last
+ *             wave under 90% full (int8 GEMMs only: their int32 sums are exact
+ *             in any order)
+ * Returns 0, or ROCKET_E_SHAPE for a value outside these. */
+int rocket_b200_gemm_policy(int variant, int stream_k);
+
 #ifdef __cplusplus
 }
 #endif

@@ -157,6 +157,7 @@ _SIGS += [
     ("rocket_stream_free", None, [_P]),
     ("rocket_matmul_fp16_stream", c_int, [_P, c_int, c_int, c_int, _P, _P, _P]),
     ("rocket_matmul_fp16_stream_fused", c_int, [_P, c_int, c_int, _P, _P, c_int, _P, _P]),
+    ("rocket_b200_gemm_policy", c_int, [c_int, c_int]),
     ("rocket_fa_ctx_create", _P, [c_int]),
     ("rocket_fa_ctx_free", None, [_P]),
     ("rocket_flash_attn_fp16", c_int, [c_int] * 7 + [c_float, c_float] + [_P] * 5),

@@ -22,8 +22,10 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <mutex>
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
+#include <cstring>
 
 #include "rkb_ptx.cuh"
 #include "rkb_tmap.h"
@@ -59,7 +61,7 @@ template <> struct Kind<RKB_IN_I8> {
 constexpr int BM = 128;            // UMMA M (cta_group::1)
 constexpr int BK_BYTES = 128;      // one 128-byte swizzle row per K-block
 constexpr int NUM_THREADS = 192;   // 6 warps
-constexpr int PREFETCH = 12;       // K-blocks of L2 prefetch ahead of the current load
+constexpr int PREFETCH = 12;       // default K-blocks of L2 prefetch ahead of the current load
 
 template <int BN>
 struct Cfg {
@@ -68,8 +70,9 @@ struct Cfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (BN == 256) ? 4 : 6;
     static constexpr int TMEM_COLS = 2 * BN;   // two accumulators
+    static constexpr int STG_BYTES = 4 * 2 * 4096;   // epilogue: 4 warps x 2 chunk buffers
     static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + 1024;
 };
 
 struct Args {
@@ -85,6 +88,13 @@ struct Args {
     int act;
     int k_splits, kb_per_split;   // split-K: unit t -> (split, tile); partials at C + split*split_stride
     long split_stride;
+    int tma_store;                // C written through the tensor map (staged, full lines)
+    int prefetch;                 // K-blocks of L2 prefetch ahead (0 = none)
+    // stream-K tail (pair kernel): sk_W full waves of whole tiles, then the
+    // K-iterations of the remaining sk_R tiles split evenly, sk_L per pair
+    int sk, sk_W, sk_R, sk_L;
+    void *sk_part;                // per tail tile a 256 x BN sum buffer (zeroed per launch)
+    int *sk_cnt;                  // per tail tile 8 arrival counters (zeroed per launch)
     int *err;
 };
 
@@ -92,6 +102,80 @@ RKB_DEV float apply_act(float v, int act) {
     if (act == RKB_ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
     if (act == RKB_ACT_SILU) return v / (1.0f + expf(-v));
     return v;
+}
+
+// Output words of 32 consecutive columns of one row with the fused epilogue
+// applied: 32 words for 4-byte outputs, 16 (fp16 pairs) for fp16.  Rows past M
+// and vectors past N read nothing; their words are never stored.
+template <int OUT>
+RKB_DEV void pack_chunk(const Args &g, int row, int col, uint32_t (&r)[32]) {
+    const bool in = row < g.M;
+    if (OUT == RKB_OUT_I32) return;
+    const float rs = (in && g.row_scale) ? g.row_scale[row] : 1.0f;
+    if (OUT == RKB_OUT_F32) {
+        if (!g.row_scale && !g.col_scale) return;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const float cs = (g.col_scale && col + j < g.N) ? g.col_scale[col + j] : 1.0f;
+            r[j] = __float_as_uint(__uint_as_float(r[j]) * rs * cs);
+        }
+        return;
+    }
+    const __half *res = (in && g.residual) ? g.residual + static_cast<long>(row) * g.ldr + col : nullptr;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        const bool vin = col + 8 * v + 8 <= g.N;
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float a = __uint_as_float(r[8 * v + j]) * rs;
+            if (g.col_scale && vin) a *= g.col_scale[col + 8 * v + j];
+            if (g.bias && vin) a += __half2float(g.bias[col + 8 * v + j]);
+            f[j] = apply_act(a, g.act);
+        }
+        if (res && vin) {
+            const uint4 rv = *reinterpret_cast<const uint4 *>(res + 8 * v);
+            const __half *rh = reinterpret_cast<const __half *>(&rv);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] += __half2float(rh[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            __half2 p = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+            r[4 * v + j] = *reinterpret_cast<uint32_t *>(&p);
+        }
+    }
+}
+
+// Stage one packed 32-row x 32-column chunk (this warp's rows) in the swizzled
+// layout the C tensor map expects -- 128-byte rows with the 128-byte swizzle for
+// 4-byte outputs, 64-byte rows with the 64-byte swizzle for fp16 -- and store it
+// with one TMA instruction.  Both patterns keep the one-row-per-thread writes
+// free of bank conflicts.
+template <int OUT>
+RKB_DEV void stage_store(const CUtensorMap *tmC, uint32_t buf, int lane, const uint32_t (&w)[32],
+                         int col, int row0) {
+    if (OUT == RKB_OUT_F16) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t a = buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[4 * j]), "r"(w[4 * j + 1]),
+                         "r"(w[4 * j + 2]), "r"(w[4 * j + 3]) : "memory");
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t a = buf + lane * 128 + ((j ^ (lane & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(w[4 * j]), "r"(w[4 * j + 1]),
+                         "r"(w[4 * j + 2]), "r"(w[4 * j + 3]) : "memory");
+        }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(tmC, buf, col, row0);
+        bulk_commit();
+    }
 }
 
 template <int OUT>
@@ -161,7 +245,7 @@ RKB_DEV void store_chunk(const Args &g, int row, int col, const uint32_t (&r)[32
 template <int KIND, int OUT, int BN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-            const Args g) {
+            const __grid_constant__ CUtensorMap tmC, const Args g) {
     using C = Cfg<BN>;
     constexpr int STAGES = C::STAGES;
     constexpr int BK_ELEMS = BK_BYTES / Kind<KIND>::ESIZE;
@@ -172,9 +256,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES + C::STG_BYTES);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
     const uint32_t smem_base = smem_u32(smem);
+    const uint32_t stg_base = smem_base + STAGES * C::STAGE_BYTES;
     auto sA = [&](int s) { return smem_base + s * C::STAGE_BYTES; };
     auto sB = [&](int s) { return smem_base + s * C::STAGE_BYTES + C::A_BYTES; };
     auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
@@ -189,6 +274,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     if (threadIdx.x == 0) {
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        if (g.tma_store) prefetch_tmap(&tmC);
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
@@ -219,9 +305,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 const int mt = t % g.m_tiles, nt = t / g.m_tiles;
                 for (int kb = 0; kb < g.k_blocks; ++kb) {
-                    if (kb + PREFETCH < g.k_blocks) {   // L2 prefetch beyond the ring
-                        tma_prefetch_2d(&tmA, (kb + PREFETCH) * BK_ELEMS, mt * BM);
-                        tma_prefetch_2d(&tmB, (kb + PREFETCH) * BK_ELEMS, nt * BN);
+                    if (g.prefetch && kb + g.prefetch < g.k_blocks) {   // L2 prefetch beyond the ring
+                        tma_prefetch_2d(&tmA, (kb + g.prefetch) * BK_ELEMS, mt * BM);
+                        tma_prefetch_2d(&tmB, (kb + g.prefetch) * BK_ELEMS, nt * BN);
                     }
                     if (!mbar_wait(empty_bar(s), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) { ok = false; break; }
                     mbar_arrive_expect_tx(full_bar(s), C::STAGE_BYTES);
@@ -271,6 +357,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     } else {
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         int it = 0;
+        uint32_t nstore = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
             const int b = it & 1;
             const uint32_t aph = (it >> 1) & 1;
@@ -279,6 +366,27 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const int mt = t % g.m_tiles, nt = t / g.m_tiles;
             const int row = mt * BM + q * 32 + lane;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
+            if (g.tma_store) {
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c, r);
+                    tmem_ld_wait();
+                    if (c + 32 == BN) {   // accumulator drained: release it before the last store
+                        tc_fence_before();
+                        mbar_arrive(tempty_bar(b));
+                    }
+                    const int col = nt * BN + c;
+                    if (col >= g.N) continue;
+                    pack_chunk<OUT>(g, row, col, r);
+                    const uint32_t buf = stg_base + (q * 2 + (nstore & 1)) * 4096;
+                    if (lane == 0) bulk_wait_read<1>();   // the store that used buf has read it
+                    __syncwarp();
+                    stage_store<OUT>(&tmC, buf, lane, r, col, row - lane);
+                    ++nstore;
+                }
+                continue;
+            }
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 uint32_t r[32];
@@ -290,6 +398,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             tc_fence_before();
             mbar_arrive(tempty_bar(b));
         }
+        if (lane == 0 && g.tma_store) bulk_wait<0>();
     }
 
     tc_fence_before();
@@ -298,6 +407,59 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         tc_fence_after();
         tmem_dealloc(tmem_base, C::TMEM_COLS);
     }
+}
+
+// Tensor map for the staged TMA-store epilogue: 32 x 32 boxes, 128-byte swizzle
+// for 4-byte outputs, 64-byte for fp16.  Returns 1 when C can be written that way
+// (16-byte aligned base and row pitch), else 0 and the kernel stores directly.
+// ROCKET_GEMM_DIRECT_STORE=1 forces direct stores (for comparison).
+// Stream-K tail plan for the pair kernel: when whole tiles leave the last
+// wave under 90% full, the K-iterations of the tail tiles are spread over all
+// pairs.  ROCKET_GEMM_STREAMK=0 turns it off.
+struct SkPlan {
+    int on, P, W, R, L;
+    size_t part_bytes, cnt_bytes;
+};
+inline SkPlan sk_plan(int M, int N, int K, int esize, int BN, int sms) {
+    static const int env = getenv("ROCKET_GEMM_STREAMK") ? atoi(getenv("ROCKET_GEMM_STREAMK")) : 1;
+    SkPlan p{};
+    const int P = sms / 2;
+    // int8 only: its int32 sums are exact in any order; float sums would depend
+    // on the order the segments arrive in
+    if (!env || esize != 1 || P < 1) return p;
+    const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
+    const int kb = (K * esize + BK_BYTES - 1) / BK_BYTES;
+    if (tiles % P == 0) return p;
+    const int waves = (tiles + P - 1) / P;
+    if (tiles >= 0.9 * waves * P) return p;
+    p.P = P;
+    p.W = tiles / P;
+    p.R = tiles - p.W * P;
+    p.L = (p.R * kb + P - 1) / P;
+    if (p.L < 4) return SkPlan{};
+    p.on = 1;
+    p.part_bytes = static_cast<size_t>(p.R) * 2 * BM * BN * 4;
+    p.cnt_bytes = (static_cast<size_t>(p.R) * 8 * 4 + 255) & ~static_cast<size_t>(255);
+    return p;
+}
+
+// L2 prefetch distance in K-blocks (ROCKET_GEMM_PREFETCH, default PREFETCH)
+inline int prefetch_distance() {
+    static const int v = getenv("ROCKET_GEMM_PREFETCH") ? atoi(getenv("ROCKET_GEMM_PREFETCH")) : PREFETCH;
+    return v < 0 ? 0 : v;
+}
+
+template <int OUT>
+int c_store_map(CUtensorMap *tc, int M, int N, void *C, long ldc) {
+    static const int off = getenv("ROCKET_GEMM_DIRECT_STORE") ? atoi(getenv("ROCKET_GEMM_DIRECT_STORE")) : 0;
+    memset(tc, 0, sizeof *tc);
+    const int osize = OUT == RKB_OUT_F16 ? 2 : 4;
+    if (off || (reinterpret_cast<uintptr_t>(C) & 15) || ((ldc * osize) & 15)) return 0;
+    const CUtensorMapDataType odt = OUT == RKB_OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                  : OUT == RKB_OUT_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                       : CU_TENSOR_MAP_DATA_TYPE_INT32;
+    const CUtensorMapSwizzle sw = OUT == RKB_OUT_F16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+    return make_tmap_2d(tc, C, odt, osize, N, M, ldc, 32, 32, sw) == 0 ? 1 : 0;
 }
 
 template <int KIND, int OUT, int BN>
@@ -328,16 +490,73 @@ int launch(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
     g.ldr = d->ldr; g.act = d->act;
     g.k_splits = 1; g.kb_per_split = g.k_blocks; g.split_stride = 0;
     g.err = err;
+    CUtensorMap tc;
+    g.tma_store = c_store_map<OUT>(&tc, d->M, d->N, g.C, g.ldc);
+    g.prefetch = prefetch_distance();
     const int tiles = g.m_tiles * g.n_tiles;
     const int sms = rkb_device_sm_count(dev);
     const int grid = tiles < sms ? tiles : sms;
-    gemm_kernel<KIND, OUT, BN><<<grid, NUM_THREADS, C::SMEM, stream>>>(ta, tb, g);
+    gemm_kernel<KIND, OUT, BN><<<grid, NUM_THREADS, C::SMEM, stream>>>(ta, tb, tc, g);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         fprintf(stderr, "rkb gemm launch: %s\n", cudaGetErrorString(e));
         return ROCKET_E_DEVICE;
     }
     return 0;
+}
+
+
+// Work units of one CTA pair: (tile, K-block range).  Without stream-K: tiles
+// pair, pair + P, ... (with the opt-in split-K ranges).  With stream-K: sk_W
+// whole tiles per pair, then this pair's contiguous share of the tail's
+// flattened (tile, K-block) iterations, cut at tile boundaries.  A cut tile
+// ("split" unit) is finished by whichever of its segments arrives last.
+// Stream-K sum buffers: per tail tile 256 rows x BN words, word-interleaved so
+// that warp w of CTA r adds and reads its 32 rows x 32-column chunk c with
+// coalesced 128-byte lines: word ((((r * 4 + w) * (BN / 32) + c) * 32 + j) * 32 + lane).
+struct Unit {
+    int tile, k0, k1;
+    int split, slot, tl;      // stream-K: split segment, its partial slot, tail tile index
+};
+struct UnitIter {
+    int pair, P, i, it, end;
+};
+RKB_DEV void units_begin(const Args &g, int pair, int P, UnitIter &u) {
+    u.pair = pair; u.P = P; u.i = 0;
+    u.it = pair * g.sk_L;
+    const int tot = g.sk_R * g.k_blocks;
+    u.end = u.it + g.sk_L < tot ? u.it + g.sk_L : tot;
+}
+RKB_DEV bool units_next(const Args &g, int mn_tiles, UnitIter &s, Unit &u) {
+    u.split = 0; u.slot = 0; u.tl = 0;
+    if (!g.sk) {
+        const int t = s.pair + s.i * s.P;
+        if (t >= mn_tiles * g.k_splits) return false;
+        ++s.i;
+        u.tile = t % mn_tiles;
+        u.k0 = (t / mn_tiles) * g.kb_per_split;
+        const int e = u.k0 + g.kb_per_split;
+        u.k1 = e < g.k_blocks ? e : g.k_blocks;
+        u.tl = t / mn_tiles;   // split-K slab index
+        return true;
+    }
+    if (s.i < g.sk_W) {
+        u.tile = s.pair + s.i * s.P;
+        ++s.i;
+        u.k0 = 0; u.k1 = g.k_blocks;
+        return true;
+    }
+    if (s.it >= s.end) return false;
+    const int kb = g.k_blocks;
+    const int tau = s.it / kb, k0 = s.it % kb;
+    const int k1 = k0 + (s.end - s.it) < kb ? k0 + (s.end - s.it) : kb;
+    u.tile = g.sk_W * s.P + tau;
+    u.k0 = k0; u.k1 = k1;
+    u.split = !(k0 == 0 && k1 == kb);
+    u.slot = 2 * s.pair + (s.it == s.pair * g.sk_L ? 0 : 1);
+    u.tl = tau;
+    s.it += k1 - k0;
+    return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -356,14 +575,15 @@ struct Cfg2 {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (BN == 256) ? 6 : 8;
     static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int STG_BYTES = 4 * 2 * 4096;   // epilogue: 4 warps x 2 chunk buffers
     static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + 1024;
 };
 
 template <int KIND, int OUT, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-             const Args g) {
+             const __grid_constant__ CUtensorMap tmC, const Args g) {
     using C = Cfg2<BN>;
     constexpr int STAGES = C::STAGES;
     constexpr int BK_ELEMS = BK_BYTES / Kind<KIND>::ESIZE;
@@ -372,9 +592,10 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES + C::STG_BYTES);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
     const uint32_t smem_base = smem_u32(smem);
+    const uint32_t stg_base = smem_base + STAGES * C::STAGE_BYTES;
     auto sA = [&](int s) { return smem_base + s * C::STAGE_BYTES; };
     auto sB = [&](int s) { return smem_base + s * C::STAGE_BYTES + C::A_BYTES; };
     auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
@@ -392,6 +613,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     if (threadIdx.x == 0) {
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        if (g.tma_store) prefetch_tmap(&tmC);
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
@@ -413,28 +635,24 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     const uint32_t tmem_base = *tmem_slot;
 
     const int mn_tiles = g.m_tiles * g.n_tiles;
-    const int num_tiles = mn_tiles * g.k_splits;
     const int cluster_id = blockIdx.x >> 1;
     const int nclusters = gridDim.x >> 1;
-    auto kb_lo = [&](int t) { return (t / mn_tiles) * g.kb_per_split; };
-    auto kb_hi = [&](int t) {
-        const int e = (t / mn_tiles + 1) * g.kb_per_split;
-        return e < g.k_blocks ? e : g.k_blocks;
-    };
 
     if (warp == 0) {
         if (lane == 0) {
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int t = cluster_id; t < num_tiles && ok; t += nclusters) {
-                const int tt = t % mn_tiles;
-                const int mt = tt % g.m_tiles, nt = tt / g.m_tiles;
-                const int kb1 = kb_hi(t);
-                for (int kb = kb_lo(t); kb < kb1; ++kb) {
-                    if (kb + PREFETCH < kb1) {
-                        tma_prefetch_2d(&tmA, (kb + PREFETCH) * BK_ELEMS, mt * 2 * BM + rank * BM);
-                        tma_prefetch_2d(&tmB, (kb + PREFETCH) * BK_ELEMS, nt * BN + rank * C::BNH);
+            UnitIter ui;
+            units_begin(g, cluster_id, nclusters, ui);
+            Unit un;
+            while (ok && units_next(g, mn_tiles, ui, un)) {
+                const int mt = un.tile % g.m_tiles, nt = un.tile / g.m_tiles;
+                const int kb1 = un.k1;
+                for (int kb = un.k0; kb < kb1; ++kb) {
+                    if (g.prefetch && kb + g.prefetch < kb1) {
+                        tma_prefetch_2d(&tmA, (kb + g.prefetch) * BK_ELEMS, mt * 2 * BM + rank * BM);
+                        tma_prefetch_2d(&tmB, (kb + g.prefetch) * BK_ELEMS, nt * BN + rank * C::BNH);
                     }
                     if (!mbar_wait(empty_bar(s), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) { ok = false; break; }
                     const uint32_t lf = mapa_shared(full_bar(s), 0);
@@ -451,13 +669,16 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
             uint32_t ph = 0;
             bool ok = true;
             int it = 0;
-            for (int t = cluster_id; t < num_tiles && ok; t += nclusters, ++it) {
+            UnitIter ui;
+            units_begin(g, cluster_id, nclusters, ui);
+            Unit un;
+            for (; ok && units_next(g, mn_tiles, ui, un); ++it) {
                 const int b = it & 1;
                 const uint32_t aph = (it >> 1) & 1;
                 if (!mbar_wait(tempty_bar(b), aph ^ 1, g.err, ERR_WAIT_MMA_ACC)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t dcol = tmem_base + b * BN;
-                const int kb0 = kb_lo(t), kb1 = kb_hi(t);
+                const int kb0 = un.k0, kb1 = un.k1;
                 for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(full_bar(s), ph, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
                     tc_fence_after();
@@ -488,32 +709,101 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     } else {
         const int q = warp & 3;
         int it = 0;
+        uint32_t nstore = 0;
         const uint32_t lempty0 = mapa_shared(tempty_bar(0), 0);
         const uint32_t lempty1 = mapa_shared(tempty_bar(1), 0);
-        for (int t = cluster_id; t < num_tiles; t += nclusters, ++it) {
+        UnitIter ui;
+        units_begin(g, cluster_id, nclusters, ui);
+        Unit un;
+        for (; units_next(g, mn_tiles, ui, un); ++it) {
             const int b = it & 1;
             const uint32_t aph = (it >> 1) & 1;
             if (!mbar_wait(tfull_bar(b), aph, g.err, ERR_WAIT_EPILOGUE)) break;
             tc_fence_after();
-            const int tt = t % mn_tiles;
-            const int mt = tt % g.m_tiles, nt = tt / g.m_tiles;
+            const int mt = un.tile % g.m_tiles, nt = un.tile / g.m_tiles;
             const int row = mt * 2 * BM + rank * BM + q * 32 + lane;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
             Args gs = g;   // split-K partial slab of this unit
             if (g.k_splits > 1)
-                gs.C = static_cast<float *>(g.C) + static_cast<long>(t / mn_tiles) * g.split_stride;
+                gs.C = static_cast<float *>(g.C) + static_cast<long>(un.tl) * g.split_stride;
+            // stream-K split segment: add the accumulator into the tile's sum buffer
+            // (fire-and-forget reductions, exact in int32), release TMEM, count in;
+            // the last of the tile's segments to arrive reads the sum and stores C
+            bool from_sum = false;
+            const uint32_t *sum_w = nullptr;
+            if (un.split) {
+                uint32_t *acc = static_cast<uint32_t *>(g.sk_part) +
+                                (static_cast<size_t>(un.tl) * 2 * BM * BN) +
+                                static_cast<size_t>(rank * 4 + q) * (BN / 32) * 1024 + lane;
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) atomicAdd(acc + (c / 32) * 1024 + j * 32, r[j]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(b ? lempty1 : lempty0);
+                const int kb = g.k_blocks;
+                const int nseg = (un.tl * kb + kb - 1) / g.sk_L - (un.tl * kb) / g.sk_L + 1;
+                int last = 0;
+                if (lane == 0) {
+                    __threadfence();
+                    last = atomicAdd(g.sk_cnt + un.tl * 8 + rank * 4 + q, 1) == nseg - 1;
+                    if (last) __threadfence();
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (!last) continue;
+                from_sum = true;
+                sum_w = acc;
+            }
+            // 32 words of this warp's rows for chunk c: from TMEM, or from the sum buffer
+            auto load_chunk = [&](uint32_t (&r)[32], int c) {
+                if (from_sum) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) r[j] = __ldcg(sum_w + (c / 32) * 1024 + j * 32);
+                } else {
+                    tmem_ld32(tbase + c, r);
+                    tmem_ld_wait();
+                }
+            };
+            if (g.tma_store) {
+                const int row0 = row - lane;
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    uint32_t r[32];
+                    load_chunk(r, c);
+                    if (c + 32 == BN && !from_sum) {   // accumulator drained: release it before the last store
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive_cluster(b ? lempty1 : lempty0);
+                    }
+                    const int col = nt * BN + c;
+                    if (col >= g.N) continue;
+                    pack_chunk<OUT>(g, row, col, r);
+                    const uint32_t buf = stg_base + (q * 2 + (nstore & 1)) * 4096;
+                    if (lane == 0) bulk_wait_read<1>();   // the store that used buf has read it
+                    __syncwarp();
+                    stage_store<OUT>(&tmC, buf, lane, r, col, row0);
+                    ++nstore;
+                }
+                continue;
+            }
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 uint32_t r[32];
-                tmem_ld32(tbase + c, r);
-                tmem_ld_wait();
+                load_chunk(r, c);
                 const int col = nt * BN + c;
                 if (col < g.N) store_chunk<OUT>(gs, row, col, r);
             }
+            if (from_sum) continue;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(b ? lempty1 : lempty0);
         }
+        if (lane == 0 && g.tma_store) bulk_wait<0>();
     }
 
     tc_fence_before();
@@ -524,8 +814,10 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     }
 }
 
+
+
 template <int KIND, int OUT, int BN>
-int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream, int splits = 1) {
+int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream, int splits = 1, int use_sk = 0) {
     using C = Cfg2<BN>;
     static std::once_flag attr_once[16];
     int dev = 0;
@@ -561,10 +853,28 @@ int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream, int splits = 
         g.act = RKB_ACT_NONE;
     }
     g.err = err;
+    // staged TMA stores of C (not for split-K slabs: a tile past M would spill
+    // into the next slab)
+    CUtensorMap tc;
+    g.tma_store = splits == 1 ? c_store_map<OUT>(&tc, d->M, d->N, g.C, g.ldc) : 0;
+    g.prefetch = prefetch_distance();
     const int tiles = g.m_tiles * g.n_tiles * splits;
     const int pairs = rkb_device_sm_count(dev) / 2;
-    const int grid = 2 * (tiles < pairs ? tiles : pairs);
-    gemm2_kernel<KIND, OUT, BN><<<grid, NUM_THREADS, C::SMEM, stream>>>(ta, tb, g);
+    int grid = 2 * (tiles < pairs ? tiles : pairs);
+    g.sk = 0; g.sk_W = g.sk_R = g.sk_L = 0; g.sk_part = nullptr; g.sk_cnt = nullptr;
+    if (splits == 1 && use_sk && d->workspace) {
+        const SkPlan sp = sk_plan(d->M, d->N, d->K, esize, BN, rkb_device_sm_count(dev));
+        if (sp.on) {
+            g.sk = 1; g.sk_W = sp.W; g.sk_R = sp.R; g.sk_L = sp.L;
+            g.sk_part = d->workspace;
+            g.sk_cnt = reinterpret_cast<int *>(static_cast<char *>(d->workspace) + sp.part_bytes);
+            // sum buffers and arrival counters start at zero every launch
+            if (cudaMemsetAsync(d->workspace, 0, sp.part_bytes + sp.cnt_bytes, stream) != cudaSuccess)
+                return ROCKET_E_DEVICE;
+            grid = 2 * sp.P;
+        }
+    }
+    gemm2_kernel<KIND, OUT, BN><<<grid, NUM_THREADS, C::SMEM, stream>>>(ta, tb, tc, g);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         fprintf(stderr, "rkb gemm2 launch: %s\n", cudaGetErrorString(e));
@@ -573,29 +883,52 @@ int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream, int splits = 
     return 0;
 }
 
-// Kernel choice by estimated time: waves x work per tile / assumed efficiency
-// (single-CTA tiles 128 x BN, CTA-pair tiles 256 x BN on two SMs).  Returns
-// 0x100 | BN for the pair kernel, BN for the single-CTA one.
-inline int pick_variant(int M, int N) {
+
+// Kernel choice by estimated time: waves x (per-SM tile area x K-blocks) /
+// assumed efficiency, over single-CTA tiles 128 x BN and CTA-pair tiles
+// 256 x BN on two SMs.  A pair option whose last wave would run under-filled
+// may instead take the stream-K tail (sk_plan): fractional waves plus a fixed
+// cost for the zeroed sum buffers and the tail exchange (about 15 us, here
+// in the same units: 1 unit ~ 11 ps on B200).  Efficiencies and the fixed
+// cost were fitted to measured int8 GEMMs at the 12B-prefill shapes.
+// Returns 0x100 | BN for the pair kernel, BN for the single-CTA one.
+struct Pick { int code, sk; };
+// process-wide override (rocket_b200_gemm_policy); 0 / -1 = automatic
+inline std::atomic<int> &policy_variant() { static std::atomic<int> v{0}; return v; }
+inline std::atomic<int> &policy_sk() { static std::atomic<int> v{-1}; return v; }
+inline Pick pick_kernel(int M, int N, int K, int esize) {
     static const char *e = getenv("ROCKET_GEMM_VARIANT");
-    if (e) {
-        int v = atoi(e);
-        if (v == 128 || v == 256 || v == 0x180 || v == 0x200 || v == 384 || v == 512) return v == 384 ? 0x180 : v == 512 ? 0x200 : v;
+    const int kb = (K * esize + BK_BYTES - 1) / BK_BYTES;
+    const int sms = 148;
+    const int pv = policy_variant().load(std::memory_order_relaxed);
+    const int psk = policy_sk().load(std::memory_order_relaxed);
+    if (pv || e) {
+        int v = pv ? pv : atoi(e);
+        if (v == 384) v = 0x180;
+        if (v == 512) v = 0x200;
+        if (v == 128 || v == 256 || v == 0x180 || v == 0x200) {
+            const int sk = (v & 0x100) && psk != 0 ? sk_plan(M, N, K, esize, v == 0x200 ? 256 : 128, sms).on : 0;
+            return Pick{v, sk};
+        }
     }
-    const double sms = 148.0;
+    constexpr double SK_FIXED = 1.3e6;
     struct Opt { int code, tm, bn, unit; double eff; } opts[] = {
         {256, 128, 256, 1, 0.66}, {128, 128, 128, 1, 0.60},
-        {0x200, 256, 256, 2, 0.82}, {0x180, 256, 128, 2, 0.76}};
+        {0x200, 256, 256, 2, 0.82}, {0x180, 256, 128, 2, 0.55}};
     double best = 1e300;
-    int code = 256;
+    Pick pk{256, 0};
     for (const Opt &o : opts) {
         const double tiles = std::ceil(M / double(o.tm)) * std::ceil(N / double(o.bn));
         const double units = sms / o.unit;
-        const double waves = std::ceil(tiles / units);
-        const double t = waves * (double(o.tm) * o.bn / o.unit) / o.eff;
-        if (t < best * 0.999) { best = t; code = o.code; }
+        const double tile_t = double(o.tm) * o.bn / o.unit * kb / o.eff;
+        const double t_dp = std::ceil(tiles / units) * tile_t;
+        if (t_dp < best * 0.999) { best = t_dp; pk = Pick{o.code, 0}; }
+        if (o.unit == 2 && psk != 0 && sk_plan(M, N, K, esize, o.bn, sms).on) {
+            const double t_sk = tiles / units * tile_t + SK_FIXED;
+            if (t_sk < best * 0.999 || psk == 1) { best = t_sk; pk = Pick{o.code, 1}; }
+        }
     }
-    return code;
+    return pk;
 }
 
 // Split-K reduction: C = epilogue(sum over splits of the fp32 partials), the
@@ -657,9 +990,29 @@ inline int pick_splits(const rkb_gemm_desc *d) {
 }  // namespace dense
 }  // namespace rkb
 
+extern "C" int rocket_b200_gemm_policy(int variant, int stream_k) {
+    if (variant != 0 && variant != 128 && variant != 256 && variant != 384 && variant != 512) return ROCKET_E_SHAPE;
+    if (stream_k < -1 || stream_k > 1) return ROCKET_E_SHAPE;
+    rkb::dense::policy_variant().store(variant == 384 ? 0x180 : variant == 512 ? 0x200 : variant);
+    rkb::dense::policy_sk().store(stream_k);
+    return 0;
+}
+
+extern "C" int rkb_gemm_launches(const rkb_gemm_desc *d) {
+    return rkb::dense::pick_splits(d) > 1 ? 2 : 1;   // split-K adds its reduce kernel
+}
+
 extern "C" size_t rkb_gemm_workspace_bytes(const rkb_gemm_desc *d) {
-    const int s = rkb::dense::pick_splits(d);
-    return s > 1 ? static_cast<size_t>(s) * d->M * d->N * sizeof(float) : 0;
+    using namespace rkb::dense;
+    const int s = pick_splits(d);
+    if (s > 1) return static_cast<size_t>(s) * d->M * d->N * sizeof(float);
+    const int esize = d->in_kind == RKB_IN_I8 ? 1 : d->in_kind == RKB_IN_TF32 ? 4 : 2;
+    const Pick pk = pick_kernel(d->M, d->N, d->K, esize);
+    if (!pk.sk) return 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const SkPlan sp = sk_plan(d->M, d->N, d->K, esize, pk.code == 0x200 ? 256 : 128, rkb_device_sm_count(dev));
+    return sp.on ? sp.part_bytes + sp.cnt_bytes : 0;
 }
 
 extern "C" int rkb_gemm_run(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
@@ -685,11 +1038,12 @@ extern "C" int rkb_gemm_run(const rkb_gemm_desc *d, int *err, cudaStream_t strea
                                                                  stride, d->M, d->N, d->C, d->ldc, bias, d->act, res, d->ldr);
         return cudaGetLastError() == cudaSuccess ? 0 : ROCKET_E_DEVICE;
     }
-    const int v = pick_variant(d->M, d->N);
+    const Pick pk = pick_kernel(d->M, d->N, d->K, d->in_kind == RKB_IN_I8 ? 1 : d->in_kind == RKB_IN_TF32 ? 4 : 2);
+    const int v = pk.code;
 #define RKB_DISPATCH(KIND, OUT)                                                   \
     switch (v) {                                                                  \
-    case 0x200: return launch2<KIND, OUT, 256>(d, err, stream);                   \
-    case 0x180: return launch2<KIND, OUT, 128>(d, err, stream);                   \
+    case 0x200: return launch2<KIND, OUT, 256>(d, err, stream, 1, pk.sk);         \
+    case 0x180: return launch2<KIND, OUT, 128>(d, err, stream, 1, pk.sk);         \
     case 128:   return launch<KIND, OUT, 128>(d, err, stream);                    \
     default:    return launch<KIND, OUT, 256>(d, err, stream);                    \
     }

@@ -137,6 +137,21 @@ RKB_DEV void prefetch_tmap(const CUtensorMap *tm) {
 RKB_DEV void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// 2D tiled TMA store shared -> global (out-of-range rows / columns are not
+// written), tracked by bulk async-groups of the issuing thread.
+RKB_DEV void tma_store_2d(const CUtensorMap *tm, uint32_t src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(tm)), "r"(src), "r"(c0), "r"(c1) : "memory");
+}
+RKB_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N of this thread's bulk groups still read shared memory
+template <int N> RKB_DEV void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// wait until at most N of this thread's bulk groups are incomplete
+template <int N> RKB_DEV void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // ---- tcgen05 -------------------------------------------------------------------
 RKB_DEV void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {

@@ -108,7 +108,7 @@ void rkb_call_gemm(rkb_call *c, int M, int N, int K, const void *A, long lda, co
     d.bias = bias; d.act = act; d.residual = res; d.ldr = ldr;
     const size_t wb = rkb_gemm_workspace_bytes(&d);
     if (wb && !(d.workspace = rkb_call_tmp(c, wb))) return;
-    rkb_count(0, wb ? 2 : 1);
+    rkb_count(0, rkb_gemm_launches(&d));
     int ps = rkb_prof_begin(c->h);
     rkb_call_check(c, rkb_gemm_run(&d, c->h->err_dev, c->h->stream));
     rkb_prof_end(c->h, ps, RKB_K_GEMM_F16);
@@ -126,7 +126,7 @@ void rkb_call_gemm_kind(rkb_call *c, int in_kind, int out_kind, int M, int N, in
     d.A = A; d.lda = lda; d.B = B; d.ldb = ldb; d.C = C; d.ldc = ldc;
     const size_t wb = rkb_gemm_workspace_bytes(&d);
     if (wb && !(d.workspace = rkb_call_tmp(c, wb))) return;
-    rkb_count(0, wb ? 2 : 1);
+    rkb_count(0, rkb_gemm_launches(&d));
     int ps = rkb_prof_begin(c->h);
     rkb_call_check(c, rkb_gemm_run(&d, c->h->err_dev, c->h->stream));
     rkb_prof_end(c->h, ps, in_kind == RKB_IN_I8 ? RKB_K_GEMM_I8 : RKB_K_GEMM_F16);

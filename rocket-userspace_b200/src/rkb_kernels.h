@@ -44,6 +44,8 @@ typedef struct {
 
 /* Device workspace rkb_gemm_run will use for this descriptor (0 = none). */
 size_t rkb_gemm_workspace_bytes(const rkb_gemm_desc *d);
+/* kernels one rkb_gemm_run launches (2 with split-K's reduce) */
+int rkb_gemm_launches(const rkb_gemm_desc *d);
 
 enum rkb_act { RKB_ACT_NONE = 0, RKB_ACT_GELU = 1, RKB_ACT_SILU = 2 };
 

@@ -66,7 +66,7 @@ int rkb_dense_on(rkb_handle *h, int in_kind, int out_kind, int M, int N, int K,
     d.A = dA; d.lda = lda; d.B = dB; d.ldb = ldb; d.C = dC; d.ldc = ldc;
     const size_t wb = rkb_gemm_workspace_bytes(&d);
     if (wb && !(d.workspace = rkb_scratch(h, RKB_SCR_SPLIT, wb))) return ROCKET_E_NOMEM;
-    rkb_count(0, wb ? 2 : 1);
+    rkb_count(0, rkb_gemm_launches(&d));
     int ps = rkb_prof_begin(h);
     int rc = rkb_gemm_run(&d, h->err_dev, h->stream);
     rkb_prof_end(h, ps, in_kind == RKB_IN_F16 ? RKB_K_GEMM_F16 : RKB_K_GEMM_I8);

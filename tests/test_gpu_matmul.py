@@ -222,3 +222,70 @@ def test_fp16_small_m_split_k(dev, orc, M, K, N, monkeypatch):
     rows = list(range(0, M, max(1, M // 16))) + [M - 1]
     R, _ = orc.matmul_fp16(A[rows], B, nthreads=8)
     close_enough(orc, C1.cpu().numpy()[rows].astype(np.float32), R)
+
+
+# ---------------------------------------------------------------- stream-K tail
+# When CTA-pair tiles leave the last wave under-filled, int8 GEMMs may run the
+# stream-K tail: the tail tiles' K-blocks are split over all SM pairs, every
+# segment adds its int32 accumulator into the tile's zeroed sum buffer, and the
+# last segment to arrive stores C.  Exact in any arrival order.  The policy is
+# forced here (rocket_b200_gemm_policy) so small shapes take that path too.
+@pytest.fixture
+def force_sk(rkb):
+    def force(variant):
+        assert rkb.lib.rocket_b200_gemm_policy(variant, 1) == 0
+    yield force
+    rkb.lib.rocket_b200_gemm_policy(0, -1)
+
+
+@pytest.mark.parametrize("variant,M,K,N", [(512, 1000, 1024, 3840),    # one partial wave: 60 tiles on 74 pairs
+                                           (512, 2048, 2048, 3840),    # 1.62 waves
+                                           (384, 900, 2048, 2016),     # ragged M and N edges, 256 x 128 tiles
+                                           (512, 4096, 3840, 3840)])   # o_proj shape, 3.24 waves
+def test_int8_stream_k_exact(rkb, dev, orc, force_sk, variant, M, K, N):
+    force_sk(variant)
+    A = orc.uniform_i8(M + 5, -127, 127, (M, K))
+    B = orc.uniform_i8(N + 6, -127, 127, (N, K))
+    C = np.full((M, N), -0x55555556, np.int32)
+    for _ in range(2):      # the sum buffers must start from zero on every launch
+        assert dev.matmul_int8(M, K, N, A, B, C) == 0
+    assert np.array_equal(C, orc.matmul_int8(A, B, nthreads=16))
+
+
+def test_int8_stream_k_down_shape_rows(dev, orc):
+    """Config-5 down GEMM (4096 x 15360 x 3840) under the automatic policy, which
+    takes the stream-K tail at this shape; exact on sampled rows."""
+    import torch
+    M, K, N = 4096, 15360, 3840
+    A = orc.uniform_i8(41, -127, 127, (M, K))
+    B = orc.uniform_i8(42, -127, 127, (N, K))
+    dC = torch.empty((M, N), dtype=torch.int32, device="cuda")
+    assert dev.matmul_int8(M, K, N, torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), dC) == 0
+    C = dC.cpu().numpy()
+    rows = [0, 1, 127, 128, 255, 256, 1000, 2047, 3583, 3584, 3840, 4095]
+    assert np.array_equal(C[rows], orc.matmul_int8(A[rows], B, nthreads=16))
+
+
+def test_gemm_policy_rejects_unknown_values(rkb):
+    assert rkb.lib.rocket_b200_gemm_policy(320, -1) != 0
+    assert rkb.lib.rocket_b200_gemm_policy(0, 2) != 0
+    assert rkb.lib.rocket_b200_gemm_policy(0, -1) == 0
+
+
+@pytest.mark.parametrize("M,K,N", [(1000, 1024, 3840), (900, 2048, 2016)])
+def test_fp16_pair_tiles_ragged(rkb, dev, orc, M, K, N):
+    """fp16 / fp32-out through the pair kernel with ragged M / N edges (fp16 never
+    takes stream-K: float sums would depend on arrival order)."""
+    A = orc.normal_f16(M + 7, 1.0 / np.sqrt(K), (M, K))
+    B = orc.normal_f16(N + 8, 1.0, (N, K))
+    C = np.zeros((M, N), np.float16)
+    assert dev.matmul_fp16(M, K, N, A, B, C) == 0
+    R, _ = orc.matmul_fp16(A, B, nthreads=16)
+    fro, mar = close_enough(orc, C.astype(np.float32), R)
+    assert fro < 1e-3
+    import ctypes
+    C32 = np.zeros((M, N), np.float32)
+    assert rkb.lib.rocket_matmul_fp16_f32out(dev.fd, M, K, N, ctypes.c_void_p(A.ctypes.data),
+                                             ctypes.c_void_p(B.ctypes.data), ctypes.c_void_p(C32.ctypes.data)) == 0
+    ref = A.astype(np.float64) @ B.astype(np.float64).T
+    assert np.max(np.abs(C32 - ref)) <= 1e-4 * np.max(np.abs(ref))
