@@ -379,8 +379,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     const int col = nt * BN + c;
                     if (col >= g.N) continue;
                     pack_chunk<OUT>(g, row, col, r);
-                    const uint32_t buf = stg_base + (q * 2 + (nstore & 1)) * 4096;
-                    if (lane == 0) bulk_wait_read<1>();   // the store that used buf has read it
+                    // fp16 chunks are 2 KB: four buffers in the warp's 8 KB, else two
+                    constexpr int NBUF = OUT == RKB_OUT_F16 ? 4 : 2;
+                    const uint32_t buf = stg_base + q * 8192 + (nstore % NBUF) * (8192 / NBUF);
+                    if (lane == 0) bulk_wait_read<NBUF - 1>();   // the store that used buf has read it
                     __syncwarp();
                     stage_store<OUT>(&tmC, buf, lane, r, col, row - lane);
                     ++nstore;
@@ -409,10 +411,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
 }
 
-// Tensor map for the staged TMA-store epilogue: 32 x 32 boxes, 128-byte swizzle
-// for 4-byte outputs, 64-byte for fp16.  Returns 1 when C can be written that way
-// (16-byte aligned base and row pitch), else 0 and the kernel stores directly.
-// ROCKET_GEMM_DIRECT_STORE=1 forces direct stores (for comparison).
 // Stream-K tail plan for the pair kernel: when whole tiles leave the last
 // wave under 90% full, the K-iterations of the tail tiles are spread over all
 // pairs.  ROCKET_GEMM_STREAMK=0 turns it off.
@@ -449,12 +447,21 @@ inline int prefetch_distance() {
     return v < 0 ? 0 : v;
 }
 
+// Tensor map for the staged TMA-store epilogue: 32 x 32 boxes, 128-byte swizzle
+// for 4-byte outputs, 64-byte for fp16.  Returns 1 when C is written that way:
+// 16-byte aligned base and row pitch, and at least 16 K-blocks per tile -- with
+// shorter K the epilogue is on the critical path and the staged stores (whose
+// shared-memory reads queue behind the producer's next-tile loads on the same
+// TMA unit) measured slower than direct stores; so did fused bias / residual /
+// activation epilogues at every K tried.  ROCKET_GEMM_DIRECT_STORE=1 forces
+// direct stores, =0 staged stores whenever the layout allows.
 template <int OUT>
-int c_store_map(CUtensorMap *tc, int M, int N, void *C, long ldc) {
-    static const int off = getenv("ROCKET_GEMM_DIRECT_STORE") ? atoi(getenv("ROCKET_GEMM_DIRECT_STORE")) : 0;
+int c_store_map(CUtensorMap *tc, int M, int N, void *C, long ldc, int k_blocks, bool fused) {
+    static const int env = getenv("ROCKET_GEMM_DIRECT_STORE") ? atoi(getenv("ROCKET_GEMM_DIRECT_STORE")) : -1;
     memset(tc, 0, sizeof *tc);
     const int osize = OUT == RKB_OUT_F16 ? 2 : 4;
-    if (off || (reinterpret_cast<uintptr_t>(C) & 15) || ((ldc * osize) & 15)) return 0;
+    if (env == 1 || (env < 0 && (k_blocks < 16 || fused))) return 0;
+    if ((reinterpret_cast<uintptr_t>(C) & 15) || ((ldc * osize) & 15)) return 0;
     const CUtensorMapDataType odt = OUT == RKB_OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                   : OUT == RKB_OUT_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                        : CU_TENSOR_MAP_DATA_TYPE_INT32;
@@ -491,7 +498,8 @@ int launch(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
     g.k_splits = 1; g.kb_per_split = g.k_blocks; g.split_stride = 0;
     g.err = err;
     CUtensorMap tc;
-    g.tma_store = c_store_map<OUT>(&tc, d->M, d->N, g.C, g.ldc);
+    g.tma_store = c_store_map<OUT>(&tc, d->M, d->N, g.C, g.ldc, g.k_blocks,
+                                  g.bias || g.residual || g.act != RKB_ACT_NONE);
     g.prefetch = prefetch_distance();
     const int tiles = g.m_tiles * g.n_tiles;
     const int sms = rkb_device_sm_count(dev);
@@ -783,8 +791,10 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
                     const int col = nt * BN + c;
                     if (col >= g.N) continue;
                     pack_chunk<OUT>(g, row, col, r);
-                    const uint32_t buf = stg_base + (q * 2 + (nstore & 1)) * 4096;
-                    if (lane == 0) bulk_wait_read<1>();   // the store that used buf has read it
+                    // fp16 chunks are 2 KB: four buffers in the warp's 8 KB, else two
+                    constexpr int NBUF = OUT == RKB_OUT_F16 ? 4 : 2;
+                    const uint32_t buf = stg_base + q * 8192 + (nstore % NBUF) * (8192 / NBUF);
+                    if (lane == 0) bulk_wait_read<NBUF - 1>();   // the store that used buf has read it
                     __syncwarp();
                     stage_store<OUT>(&tmC, buf, lane, r, col, row0);
                     ++nstore;
@@ -856,7 +866,8 @@ int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream, int splits = 
     // staged TMA stores of C (not for split-K slabs: a tile past M would spill
     // into the next slab)
     CUtensorMap tc;
-    g.tma_store = splits == 1 ? c_store_map<OUT>(&tc, d->M, d->N, g.C, g.ldc) : 0;
+    g.tma_store = splits == 1 ? c_store_map<OUT>(&tc, d->M, d->N, g.C, g.ldc, g.k_blocks,
+                                                 g.bias || g.residual || g.act != RKB_ACT_NONE) : 0;
     g.prefetch = prefetch_distance();
     const int tiles = g.m_tiles * g.n_tiles * splits;
     const int pairs = rkb_device_sm_count(dev) / 2;
