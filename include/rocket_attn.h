@@ -4,7 +4,9 @@
  * q/k/v projections on the tcgen05 GEMM (bias fused), one fused attention
  * kernel (scores, online softmax and P.V on the tensor cores, scores never
  * leave the chip), output projection with its bias fused.  head_dim
- * d / n_head must be 64 (ROCKET_E_UNSUPPORTED otherwise).  Biases may be NULL.
+ * d / n_head must be a multiple of 16 and at most 256 (ROCKET_E_UNSUPPORTED
+ * otherwise); 64 runs a kernel holding O in registers, others the flash kernel
+ * below.  Biases may be NULL.
  */
 #ifndef ROCKET_ATTN_H
 #define ROCKET_ATTN_H

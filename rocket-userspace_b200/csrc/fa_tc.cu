@@ -64,6 +64,9 @@ RKB_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: 
 
 struct Args {
     int T, n_kv, dv, n_head, gqa, dhp, nkb;
+    int q_rows, kv_rows;   // rows per head in the Q / K tensor maps (>= T / n_kv)
+    int hb;                // heads per output batch: out(h, t) = out + (h / hb) * bstride + (h % hb) * dv + t * ldo
+    long bstride, ldo;
     float scale, softcap;
     const __half *mask;
     int mask_vec;          // mask rows 16-byte aligned (n_kv % 8 == 0, aligned base)
@@ -148,14 +151,14 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
         if (lane == 0) {
             mbar_arrive_expect_tx(q_full, dhp * BQ * 128);
             for (int p = 0; p < dhp; ++p)
-                tma_load_2d(sb + pl.q + p * BQ * 128, &tmQ, p * 64, h * g.T + qt * BQ, q_full);
+                tma_load_2d(sb + pl.q + p * BQ * 128, &tmQ, p * 64, h * g.q_rows + qt * BQ, q_full);
             for (int j = 0; j < nkb; ++j) {
                 const int s = j % KV_STAGES;
                 const uint32_t ph = (j / KV_STAGES) & 1;
                 if (!mbar_wait(kv_empty(s), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) break;
                 mbar_arrive_expect_tx(kv_full(s), pl.stage);
                 for (int p = 0; p < dhp; ++p)
-                    tma_load_2d(sK(s) + p * BKV * 128, &tmK, p * 64, hk * g.n_kv + j * BKV, kv_full(s));
+                    tma_load_2d(sK(s) + p * BKV * 128, &tmK, p * 64, hk * g.kv_rows + j * BKV, kv_full(s));
                 for (int c = 0; c < NPAN; ++c)
                     tma_load_2d(sV(s) + c * dv * 128, &tmV, j * BKV + c * 64, hk * dv, kv_full(s));
             }
@@ -317,7 +320,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
         if (ok && nkb > 0 && mbar_wait_warp(o_full, (nkb - 1) & 1, g.err, ERR_WAIT_EPILOGUE)) {
             tc_fence_after();
             const float inv = 1.f / l;
-            __half *dst = g.out + (static_cast<size_t>(h) * g.T + t) * dv;
+            __half *dst = g.out + (h / g.hb) * g.bstride + (h % g.hb) * dv + static_cast<long>(t) * g.ldo;
             for (int c = 0; c < dv; c += 32) {
                 uint32_t r[32];
                 tmem_ld32(tl + O_COL + c, r);
@@ -370,26 +373,33 @@ int launch(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, 
 }  // namespace fa
 }  // namespace rkb
 
-// Q/K rows must be 16-byte aligned (dh % 8 == 0); V rows are `ldv` elements
-// apart (ldv % 8 == 0, ldv >= n_kv).  Shapes the kernel does not take return
-// ROCKET_E_UNSUPPORTED: dh > 256, dv > 256, dv % 16.
-extern "C" int rkb_flash_attn(const void *Q, const void *K, const void *V, long ldv, const void *mask,
-                              void *out, int T, int n_kv, int dh, int dv, int n_head, int n_kv_heads,
-                              float scale, float softcap, int *err, cudaStream_t stream) {
+// General form: Q rows of head h start at row h * q_rows of a [n_head * q_rows][dh]
+// array, K rows of kv head hk at hk * kv_rows of [n_kv_heads * kv_rows][dh]; V is
+// [n_kv_heads * dv] rows of ldv elements; out(h, t) = out + (h / hb) * bstride +
+// (h % hb) * dv + t * ldo.  Rows must be 16-byte aligned (dh % 8, ldv % 8, ldo % 8).
+// Shapes the kernel does not take return ROCKET_E_UNSUPPORTED: dh > 256,
+// dv > 256, dv % 16.
+extern "C" int rkb_flash_attn_ex(const void *Q, const void *K, const void *V, long ldv, const void *mask,
+                                 void *out, int T, int n_kv, int dh, int dv, int n_head, int n_kv_heads,
+                                 float scale, float softcap, int q_rows, int kv_rows, int hb, long bstride,
+                                 long ldo, int *err, cudaStream_t stream) {
     using namespace rkb::fa;
-    if (T <= 0 || n_kv <= 0 || n_head <= 0 || n_kv_heads <= 0 || n_head % n_kv_heads) return ROCKET_E_SHAPE;
-    if (dh <= 0 || dh > 256 || dh % 8 || dv <= 0 || dv > 256 || dv % 16 || ldv % 8 || ldv < n_kv)
+    if (T <= 0 || n_kv <= 0 || n_head <= 0 || n_kv_heads <= 0 || n_head % n_kv_heads || hb <= 0 ||
+        q_rows < T || kv_rows < n_kv)
+        return ROCKET_E_SHAPE;
+    if (dh <= 0 || dh > 256 || dh % 8 || dv <= 0 || dv > 256 || dv % 16 || ldv % 8 || ldv < n_kv || ldo % 8)
         return ROCKET_E_UNSUPPORTED;
     const int dhp = (dh + 63) / 64;
     const int bkv = (dhp <= 2 && dv <= 128) ? 128 : 64;
     CUtensorMap tq, tk, tv;
-    if (rkb::make_tmap_2d(&tq, Q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dh, static_cast<long>(n_head) * T, dh, 64, BQ) ||
-        rkb::make_tmap_2d(&tk, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dh, static_cast<long>(n_kv_heads) * n_kv, dh, 64, bkv) ||
+    if (rkb::make_tmap_2d(&tq, Q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dh, static_cast<long>(n_head) * q_rows, dh, 64, BQ) ||
+        rkb::make_tmap_2d(&tk, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dh, static_cast<long>(n_kv_heads) * kv_rows, dh, 64, bkv) ||
         rkb::make_tmap_2d(&tv, V, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, n_kv, static_cast<long>(n_kv_heads) * dv, ldv, 64, dv))
         return ROCKET_E_SHAPE;
     Args g;
     g.T = T; g.n_kv = n_kv; g.dv = dv; g.n_head = n_head; g.gqa = n_head / n_kv_heads;
     g.dhp = dhp; g.nkb = (n_kv + bkv - 1) / bkv;
+    g.q_rows = q_rows; g.kv_rows = kv_rows; g.hb = hb; g.bstride = bstride; g.ldo = ldo;
     g.scale = scale; g.softcap = softcap;
     g.mask = static_cast<const __half *>(mask);
     g.mask_vec = mask && (n_kv % 8 == 0) && ((reinterpret_cast<uintptr_t>(mask) & 15) == 0);
@@ -403,4 +413,13 @@ extern "C" int rkb_flash_attn(const void *Q, const void *K, const void *V, long 
         return ROCKET_E_DEVICE;
     }
     return 0;
+}
+
+// Head-major form of the reference API: Q [n_head][T][dh], K [n_kv_heads][n_kv][dh],
+// V [n_kv_heads][dv] rows of ldv elements, out [n_head][T][dv].
+extern "C" int rkb_flash_attn(const void *Q, const void *K, const void *V, long ldv, const void *mask,
+                              void *out, int T, int n_kv, int dh, int dv, int n_head, int n_kv_heads,
+                              float scale, float softcap, int *err, cudaStream_t stream) {
+    return rkb_flash_attn_ex(Q, K, V, ldv, mask, out, T, n_kv, dh, dv, n_head, n_kv_heads, scale, softcap, T,
+                             n_kv, 1, static_cast<long>(T) * dv, dv, err, stream);
 }

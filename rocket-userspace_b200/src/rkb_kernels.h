@@ -102,12 +102,18 @@ int rkb_elementwise(const void *a, const void *b, int op, int kind, size_t n, vo
 /* qkv [B*T, 3*H*dh] (row pitch ld) -> Q, K [B*H, Tp, dh], Vt [B*H, dh, Tp], zero padded */
 int rkb_split_heads(const void *qkv, long ld, int B, int T, int Tp, int H, int dh, void *Q,
                     void *K, void *Vt, cudaStream_t s);
-/* out[b*T + t, h*dh + c] = softmax(Q K^T * scale) V per (b, h); dh == 64, Tp % 128 == 0 */
 /* masked GQA flash attention (csrc/fa_tc.cu): Q [nh][T][dh], K [nkvh][n_kv][dh],
  * V [nkvh][dv] rows of ldv elements, mask [T][n_kv] or NULL, out [nh][T][dv] */
 int rkb_flash_attn(const void *Q, const void *K, const void *V, long ldv, const void *mask, void *out,
                    int T, int n_kv, int dh, int dv, int n_head, int n_kv_heads, float scale,
                    float softcap, int *err, cudaStream_t stream);
+/* general addressing: per-head row counts q_rows / kv_rows in the Q / K arrays;
+ * out(h, t) = out + (h / hb) * bstride + (h % hb) * dv + t * ldo */
+int rkb_flash_attn_ex(const void *Q, const void *K, const void *V, long ldv, const void *mask, void *out,
+                      int T, int n_kv, int dh, int dv, int n_head, int n_kv_heads, float scale,
+                      float softcap, int q_rows, int kv_rows, int hb, long bstride, long ldo, int *err,
+                      cudaStream_t stream);
+/* out[b*T + t, h*dh + c] = softmax(Q K^T * scale) V per (b, h); dh == 64, Tp % 128 == 0 */
 int rkb_attention(const void *Q, const void *K, const void *Vt, int B, int H, int T, int Tp,
                   int dh, float scale, void *out, long ldo, int *err, cudaStream_t stream);
 

@@ -234,9 +234,16 @@ static void enc_mha_core(rkb_call *c, int nb, int T, int d, int n_head, const vo
     rkb_call_check(c, rkb_split_heads(qkv, 3 * d, nb, T, Tp, n_head, dh, Q, K, Vt, c->h->stream));
     rkb_prof_end(c->h, ps, RKB_K_ELEMWISE);
     ps = rkb_prof_begin(c->h);
-    if (!c->rc)
+    /* head_dim 64: the register-resident-O kernel; other head dims: the flash
+     * kernel over the same split heads (nb * n_head heads of Tp rows, output
+     * interleaved back into ctx[token][head * dh]) */
+    if (!c->rc && dh == 64)
         rkb_call_check(c, rkb_attention(Q, K, Vt, nb, n_head, T, Tp, dh, 1.0f / sqrtf((float)dh), ctx, d,
                                    c->h->err_dev, c->h->stream));
+    else if (!c->rc)
+        rkb_call_check(c, rkb_flash_attn_ex(Q, K, Vt, Tp, NULL, ctx, T, T, dh, dh, nb * n_head, nb * n_head,
+                                            1.0f / sqrtf((float)dh), 0.0f, Tp, Tp, n_head, (long)T * d, d,
+                                            c->h->err_dev, c->h->stream));
     rkb_prof_end(c->h, ps, RKB_K_ATTN);
     rkb_count(0, 2);
 }
@@ -253,8 +260,8 @@ int rocket_mha_self_fp16(int fd, int T, int d, int n_head, const _Float16 *x, co
 {
     const char *who = "rocket_mha_self_fp16";
     if (!mha_shape_ok(T, d, n_head) || !x || !Wq || !Wk || !Wv || !Wo || !out) return ROCKET_E_SHAPE;
-    if (d / n_head != 64) {
-        ROCKET_LOGE("%s: head_dim %d unsupported (the fused kernel is built for 64)\n", who, d / n_head);
+    if ((d / n_head) % 16 || d / n_head > 256) {
+        ROCKET_LOGE("%s: head_dim %d unsupported (needs a multiple of 16, at most 256)\n", who, d / n_head);
         return ROCKET_E_UNSUPPORTED;
     }
     rkb_call c;
@@ -282,8 +289,8 @@ static int encoder_common(const char *who, int fd, int nb, int T, int d, int n_h
     if (nb < 1 || !mha_shape_ok(T, d, n_head) || d_ff < 1 || d_ff % 8 || !x || !ln1_g || !ln2_g ||
         !Wq || !Wk || !Wv || !Wo || !Wf1 || !Wf2 || !out)
         return ROCKET_E_SHAPE;
-    if (d / n_head != 64) {
-        ROCKET_LOGE("%s: head_dim %d unsupported (the fused kernel is built for 64)\n", who, d / n_head);
+    if ((d / n_head) % 16 || d / n_head > 256) {
+        ROCKET_LOGE("%s: head_dim %d unsupported (needs a multiple of 16, at most 256)\n", who, d / n_head);
         return ROCKET_E_UNSUPPORTED;
     }
     rkb_call c;

@@ -130,11 +130,36 @@ def test_mha_shapes(rkb, dev, orc, T, d, nh):
     check(orc, y, ref)
 
 
-def test_mha_unsupported_head_dim(rkb, dev, orc):
-    p = orc.encoder_params(16, 128, 4, 256, 1)   # head_dim 32
-    y = np.zeros((16, 128), np.float16)
+@pytest.mark.parametrize("T,d,nh", [(16, 128, 4),      # head_dim 32
+                                    (200, 512, 4),     # head_dim 128
+                                    (77, 512, 2)])     # head_dim 256
+def test_mha_other_head_dims(rkb, dev, orc, T, d, nh):
+    """head_dim != 64 runs the flash kernel over the split heads.  Wq / Wk are
+    drawn large enough that the softmax is far from uniform."""
+    p = orc.encoder_params(T, d, nh, 4 * d, T + d + 1)
+    p["Wq"] = orc.normal_f16(T + 901, 2.0 / np.sqrt(d), (d, d))
+    p["Wk"] = orc.normal_f16(T + 902, 2.0 / np.sqrt(d), (d, d))
+    y = np.zeros((T, d), np.float16)
     args = [P(rkb, p[k]) for k in ["x", "Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo"]]
-    assert rkb.lib.rocket_mha_self_fp16(dev.fd, 16, 128, 4, *args, P(rkb, y)) == rkb.ROCKET_E_UNSUPPORTED
+    assert rkb.lib.rocket_mha_self_fp16(dev.fd, T, d, nh, *args, P(rkb, y)) == 0
+    ref = orc.mha_self(p["x"], p["Wq"], p["bq"], p["Wk"], p["bk"], p["Wv"], p["bv"], p["Wo"], p["bo"], nh)
+    check(orc, y, ref)
+
+
+def test_mha_unsupported_head_dim(rkb, dev, orc):
+    p = orc.encoder_params(16, 160, 4, 320, 1)   # head_dim 40: not a multiple of 16
+    y = np.zeros((16, 160), np.float16)
+    args = [P(rkb, p[k]) for k in ["x", "Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo"]]
+    assert rkb.lib.rocket_mha_self_fp16(dev.fd, 16, 160, 4, *args, P(rkb, y)) == rkb.ROCKET_E_UNSUPPORTED
+
+
+def test_encoder_block_head_dim_128(rkb, dev, orc):
+    T, d, nh, dff = 96, 512, 4, 1024
+    p = orc.encoder_params(T, d, nh, dff, 11)
+    y = np.zeros((T, d), np.float16)
+    assert rkb.lib.rocket_encoder_block_fp16(dev.fd, T, d, nh, dff, P(rkb, p["x"]),
+                                             *[P(rkb, p[k]) for k in rkb.ENCODER_KEYS], 1e-5, P(rkb, y)) == 0
+    check(orc, y, orc.encoder_block(p["x"], p, nh, 1e-5))
 
 
 def test_encoder_block_golden(rkb, dev, orc, gi):
