@@ -154,7 +154,7 @@ RKB_DEV void pack_chunk(const Args &g, int row, int col, uint32_t (&r)[32]) {
 // free of bank conflicts.
 template <int OUT>
 RKB_DEV void stage_store(const CUtensorMap *tmC, uint32_t buf, int lane, const uint32_t (&w)[32],
-                         int col, int row0) {
+                         int col, int row0, int plane = -1) {
     if (OUT == RKB_OUT_F16) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -173,7 +173,8 @@ RKB_DEV void stage_store(const CUtensorMap *tmC, uint32_t buf, int lane, const u
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-        tma_store_2d(tmC, buf, col, row0);
+        if (plane < 0) tma_store_2d(tmC, buf, col, row0);
+        else tma_store_3d(tmC, buf, col, row0, plane);   // split-K slab
         bulk_commit();
     }
 }
@@ -796,7 +797,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
                     const uint32_t buf = stg_base + q * 8192 + (nstore % NBUF) * (8192 / NBUF);
                     if (lane == 0) bulk_wait_read<NBUF - 1>();   // the store that used buf has read it
                     __syncwarp();
-                    stage_store<OUT>(&tmC, buf, lane, r, col, row0);
+                    stage_store<OUT>(&tmC, buf, lane, r, col, row0, g.k_splits > 1 ? un.tl : -1);
                     ++nstore;
                 }
                 continue;
@@ -866,8 +867,14 @@ int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream, int splits = 
     // staged TMA stores of C (not for split-K slabs: a tile past M would spill
     // into the next slab)
     CUtensorMap tc;
-    g.tma_store = splits == 1 ? c_store_map<OUT>(&tc, d->M, d->N, g.C, g.ldc, g.k_blocks,
-                                                 g.bias || g.residual || g.act != RKB_ACT_NONE) : 0;
+    if (splits == 1) {
+        g.tma_store = c_store_map<OUT>(&tc, d->M, d->N, g.C, g.ldc, g.k_blocks,
+                                       g.bias || g.residual || g.act != RKB_ACT_NONE);
+    } else {   // fp32 partial slabs [splits][M][N]: a 3D map clips rows past M within each slab
+        memset(&tc, 0, sizeof tc);
+        g.tma_store = encode_tmap_3d(&tc, g.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d->N, d->M, splits, d->N,
+                                     static_cast<long>(d->M) * d->N, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B) == 0;
+    }
     g.prefetch = prefetch_distance();
     const int tiles = g.m_tiles * g.n_tiles * splits;
     const int pairs = rkb_device_sm_count(dev) / 2;
@@ -983,17 +990,27 @@ __global__ void split_reduce(const float *__restrict__ ws, int splits, long stri
     }
 }
 
-// Split count for fp16 inputs (ROCKET_GEMM_SPLITK = 2..4; default 1 = off):
-// split-K on the CTA-pair 256x256 kernel.  Opt-in because at the one shape
-// class it targets (small M, e.g. 512 x 4096 x 4096) it measured no faster
-// than the unsplit kernels; it is kept, tested, for shapes where it may be.
+// Split count for fp16 inputs: split-K over the CTA-pair 256x256 kernel with
+// fp32 partial slabs and a deterministic reduce (splits summed in index order).
+// Automatic when the pair tiles cannot fill the GPU and K is long (at least 48
+// K-blocks): splits = clamp(pairs / tiles, 2, 3).  Measured on B200, fp16
+// 512x4096x4096: 35.3 -> 26.7 us; 256x4096x4096: 32.8 -> 21.0 us;
+// 1024x4096x4096: 51 -> 43 us.  ROCKET_GEMM_SPLITK = 1..4 overrides (1 = off).
 inline int pick_splits(const rkb_gemm_desc *d) {
     if (d->in_kind != RKB_IN_F16 || d->row_scale || d->col_scale) return 1;
-    const char *e = getenv("ROCKET_GEMM_SPLITK");
-    if (!e) return 1;
-    int s = atoi(e);
     const int kblocks = (d->K * 2 + BK_BYTES - 1) / BK_BYTES;
-    if (s > 4) s = 4;   // (fp16 only)
+    const char *e = getenv("ROCKET_GEMM_SPLITK");
+    int s;
+    if (e) {
+        s = atoi(e);
+        if (s > 4) s = 4;
+    } else {
+        const int pairs = 74;
+        const int tiles = ((d->M + 2 * BM - 1) / (2 * BM)) * ((d->N + 255) / 256);
+        if (tiles >= pairs || kblocks < 48 || (d->N & 7)) return 1;
+        s = pairs / tiles;
+        s = s < 2 ? 2 : s > 3 ? 3 : s;
+    }
     while (s > 1 && kblocks / s < 4) --s;
     return s < 1 ? 1 : s;
 }

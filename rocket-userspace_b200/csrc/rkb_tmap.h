@@ -64,6 +64,23 @@ inline int encode_tmap_2d(CUtensorMap *tm, const void *base, CUtensorMapDataType
     return 0;
 }
 
+// Row-major 3D tensor [planes, rows, cols] (plane pitch and row pitch in
+// elements), box box_cols x box_rows x 1.  Not cached (split-K partial slabs only).
+inline int encode_tmap_3d(CUtensorMap *tm, const void *base, CUtensorMapDataType dt, int esize, long cols,
+                          long rows, long planes, long ld, long plane_ld, int box_cols, int box_rows,
+                          CUtensorMapSwizzle swz) {
+    auto enc = tmap_encoder();
+    if (!enc) return -1;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * esize) & 15) || ((plane_ld * esize) & 15)) return -1;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(planes)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * esize, static_cast<cuuint64_t>(plane_ld) * esize};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(tm, dt, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -1;
+}
+
 inline int make_tmap_2d(CUtensorMap *tm, const void *base, CUtensorMapDataType dt, int esize,
                         long cols, long rows, long ld, int box_cols, int box_rows,
                         CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
