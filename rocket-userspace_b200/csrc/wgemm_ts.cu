@@ -15,11 +15,19 @@
 // lane) and writes its 32 fp16 pairs with tcgen05.st, so the weights never
 // touch shared memory after their 4 KB code block lands.
 //
-// The MMA computes C^T tiles: M = 128 weight rows (A, TMEM), N = NT tokens
-// (B = activations, TMA-loaded, 128-byte swizzled).  Roles (448 threads):
-//   warp 0      producer: TMA activation tile + bulk copies of the half code
-//               block and half scale block, RS-deep raw ring
-//   warp 1      MMA issuer; two TMEM accumulators of NT columns
+// The MMA computes C^T tiles: 128 weight rows (M, A operand in TMEM) against
+// NT <= 384 tokens (B = activations, TMA-loaded, 128-byte swizzled), issued as
+// two MMAs of N = NT / 2 <= 192 that share the dequantised A tile.  The cost
+// that bounds this kernel is the dequantisation (about 2.25 instructions per
+// weight on 8 warps), so the tile is made as wide in tokens as TMEM allows:
+// every dequantised weight feeds NT MACs.  (At NT = 192 -- and equally with
+// 256 weight rows per activation tile -- ncu showed the tensor pipe 40% busy
+// with the dequant warps in fixed-latency waits.)  The accumulators take TMEM
+// columns [0, 384) single-buffered; the A ring takes [384, 512).  NT is chosen
+// per call to balance waves over the 148 SMs.  Roles (448 threads):
+//   warp 0      producer: TMA activation tile (two boxes) + bulk copies of the
+//               half code block and half scale block, RS-deep raw ring
+//   warp 1      MMA issuer: per K block 2 x 4 MMAs (one per token half)
 //   warps 2..5  epilogue: thread = weight row n, loops over tokens; every
 //               store instruction writes 32 consecutive n of one token row
 //   warps 6..13 dequantisers: warp (q, h) owns TMEM lanes 32q..32q+31 and the
@@ -31,6 +39,7 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <mutex>
+#include <cmath>
 
 #include "rkb_ptx.cuh"
 #include "rkb_tmap.h"
@@ -41,30 +50,30 @@ namespace rkb {
 namespace wts {
 
 constexpr int WM = 128;           // weight rows per tile (MMA M)
-constexpr int NT = 192;           // tokens per tile (MMA N)
+constexpr int NH_MAX = 192;       // tokens per MMA (N); a tile is two of them
 constexpr int NUM_THREADS = 448;
 constexpr int DEQ_WARP0 = 6;
 constexpr int DA = 4;             // TMEM A-ring depth (64-wide K blocks)
 constexpr int ACOLS = 32;         // TMEM columns per A tile: 128 lanes x 64 fp16
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t A_COL0 = 2 * NT;   // accumulators in [0, 2*NT), A ring after
+constexpr uint32_t A_COL0 = 2 * NH_MAX;   // accumulators in [0, 384), A ring after
 static_assert(A_COL0 + DA * ACOLS <= TMEM_COLS, "TMEM budget");
 
 template <int WBITS>
 struct Cfg {
-    static constexpr int B_BYTES = NT * 128;                          // activations, 64 fp16 per row
+    static constexpr int B_BYTES = 2 * NH_MAX * 128;                  // activations, 64 fp16 per row
     static constexpr int CODE_BYTES = WM * 64 * WBITS / 8;            // half of a 256-row block
     static constexpr int SCALE_BYTES = WM * 2 * 2;
     static constexpr int RAW_BYTES = (B_BYTES + CODE_BYTES + SCALE_BYTES + 1023) / 1024 * 1024;
-    static constexpr int TX_BYTES = B_BYTES + CODE_BYTES + SCALE_BYTES;
-    static constexpr int RS = 6;
-    static constexpr int NBARS = 2 * RS + 2 * DA + 5;
+    static constexpr int RS = WBITS == 4 ? 4 : 3;
+    static constexpr int NBARS = 2 * RS + 2 * DA + 3;
     static constexpr int SMEM = RS * RAW_BYTES + NBARS * 8 + 16 + 1024;
     static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 struct Args {
     int M, N, K;
+    int nh;                   // tokens per MMA (N); a tile covers 2 * nh tokens
     int m_tiles, n_tiles, k_blocks, kb64_total;
     const uint8_t *codes;     // resident tiled codes (256-row blocks)
     const __half *scales;     // resident tiled fp16 scales
@@ -129,8 +138,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 wgemm_ts_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
     using C = Cfg<WBITS>;
     constexpr int RS = C::RS;
-    constexpr uint32_t IDESC = idesc_f16_f32acc(WM, NT);
     constexpr int BLOCK = 256 * 64 * WBITS / 8;      // one resident 256-row x 64-K code block
+    const int nh = g.nh, nt = 2 * nh;
+    const int dstride = (nh + 31) & ~31;   // token half p at TMEM column p * dstride
+    const uint32_t IDESC = idesc_f16_f32acc(WM, nh);
+    const int tx_bytes = nt * 128 + C::CODE_BYTES + C::SCALE_BYTES;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -149,9 +161,11 @@ wgemm_ts_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
     auto raw_empty = [&](int r) { return smem_u32(&bars[RS + r]); };
     auto a_full = [&](int a) { return smem_u32(&bars[2 * RS + a]); };
     auto a_empty = [&](int a) { return smem_u32(&bars[2 * RS + DA + a]); };
-    auto tfull_bar = [&](int b) { return smem_u32(&bars[2 * RS + 2 * DA + b]); };
-    auto tempty_bar = [&](int b) { return smem_u32(&bars[2 * RS + 2 * DA + 2 + b]); };
-    const uint32_t drain_bar = smem_u32(&bars[2 * RS + 2 * DA + 4]);
+    const uint32_t tfull_bar = smem_u32(&bars[2 * RS + 2 * DA]);
+    const uint32_t tempty_bar = smem_u32(&bars[2 * RS + 2 * DA + 1]);
+    const uint32_t drain_bar = smem_u32(&bars[2 * RS + 2 * DA + 2]);
+    auto acol = [&](int a) { return A_COL0 + static_cast<uint32_t>(a * ACOLS); };
+    auto sBh = [&](int r, int p) { return sB(r) + p * NH_MAX * 128; };   // token half p (1024-aligned)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -166,10 +180,8 @@ wgemm_ts_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
             mbar_init(a_full(a), 8);
             mbar_init(a_empty(a), 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(tfull_bar(b), 1);
-            mbar_init(tempty_bar(b), 4);
-        }
+        mbar_init(tfull_bar, 1);
+        mbar_init(tempty_bar, 4);
         mbar_init(drain_bar, 1);
         fence_mbar_init();
     }
@@ -189,15 +201,16 @@ wgemm_ts_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
             uint32_t ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                const int mt = t % g.m_tiles, nt = t / g.m_tiles;   // nt: 128-row weight tile
-                const uint8_t *codes = g.codes + static_cast<size_t>(nt >> 1) * g.kb64_total * BLOCK +
-                                       (nt & 1) * C::CODE_BYTES;
-                const __half *scales = g.scales + static_cast<size_t>(nt >> 1) * g.kb64_total * 512 +
-                                       (nt & 1) * 256;
+                const int mt = t % g.m_tiles, nt128 = t / g.m_tiles;   // nt128: 128-row weight tile
+                const uint8_t *codes = g.codes + static_cast<size_t>(nt128 >> 1) * g.kb64_total * BLOCK +
+                                       (nt128 & 1) * C::CODE_BYTES;
+                const __half *scales = g.scales + static_cast<size_t>(nt128 >> 1) * g.kb64_total * 512 +
+                                       (nt128 & 1) * 256;
                 for (int kb = 0; kb < g.k_blocks; ++kb) {
                     if (!mbar_wait(raw_empty(r), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) { ok = false; break; }
-                    mbar_arrive_expect_tx(raw_full(r), C::TX_BYTES);
-                    tma_load_2d(sB(r), &tmB, kb * 64, mt * NT, raw_full(r));
+                    mbar_arrive_expect_tx(raw_full(r), tx_bytes);
+                    tma_load_2d(sBh(r, 0), &tmB, kb * 64, mt * nt, raw_full(r));
+                    tma_load_2d(sBh(r, 1), &tmB, kb * 64, mt * nt + nh, raw_full(r));
                     bulk_load(sCode(r), codes + static_cast<size_t>(kb) * BLOCK, C::CODE_BYTES, raw_full(r));
                     bulk_load(sScale(r), scales + static_cast<size_t>(kb) * 512, C::SCALE_BYTES, raw_full(r));
                     if (++r == RS) { r = 0; ph ^= 1; }
@@ -211,27 +224,26 @@ wgemm_ts_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
             bool ok = true;
             int it = 0;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
-                const int b = it & 1;
-                const uint32_t tph = (it >> 1) & 1;
-                if (!mbar_wait(tempty_bar(b), tph ^ 1, g.err, ERR_WAIT_MMA_ACC)) { ok = false; break; }
+                if (!mbar_wait(tempty_bar, (it & 1) ^ 1, g.err, ERR_WAIT_MMA_ACC)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t dcol = tmem_base + b * NT;
                 for (int kb = 0; kb < g.k_blocks; ++kb) {
                     // a_full(a) implies raw_full(r): the dequantisers waited for it
                     if (!mbar_wait(a_full(a), aph, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
                     tc_fence_after();
-                    const uint64_t bdesc = smem_desc_sw128(sB(r));
-                    const uint32_t acol = tmem_base + A_COL0 + a * ACOLS;
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        tc_mma_f16_ts(dcol, acol + k * 8, bdesc + static_cast<uint64_t>(k * 2), IDESC,
-                                      (kb | k) != 0);
+                    for (int p = 0; p < 2; ++p) {
+                        const uint64_t bdesc = smem_desc_sw128(sBh(r, p));
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            tc_mma_f16_ts(tmem_base + p * dstride, tmem_base + acol(a) + k * 8,
+                                          bdesc + static_cast<uint64_t>(k * 2), IDESC, (kb | k) != 0);
+                    }
                     tc_commit(raw_empty(r));
                     tc_commit(a_empty(a));
                     if (++r == RS) r = 0;
                     if (++a == DA) { a = 0; aph ^= 1; }
                 }
-                if (ok) tc_commit(tfull_bar(b));
+                if (ok) tc_commit(tfull_bar);
             }
             if (!ok) {
                 tc_commit(drain_bar);
@@ -239,39 +251,40 @@ wgemm_ts_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
             }
         }
     } else if (warp < DEQ_WARP0) {
-        // epilogue: lane = weight row n; TMEM columns = tokens
+        // epilogue: lane = weight row n; TMEM columns = tokens (half p at p * dstride)
         const int q = warp & 3;
         int it = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
-            const int b = it & 1;
-            const uint32_t tph = (it >> 1) & 1;
-            if (!mbar_wait_warp(tfull_bar(b), tph, g.err, ERR_WAIT_EPILOGUE)) break;
+            if (!mbar_wait_warp(tfull_bar, it & 1, g.err, ERR_WAIT_EPILOGUE)) break;
             tc_fence_after();
-            const int mt = t % g.m_tiles, nt = t / g.m_tiles;
-            const int n = nt * WM + q * 32 + lane;
-            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * NT;
+            const int mt = t % g.m_tiles, nt128 = t / g.m_tiles;
+            const int n = nt128 * WM + q * 32 + lane;
 #pragma unroll 1
-            for (int c = 0; c < NT; c += 32) {
-                uint32_t v[32];
-                tmem_ld32(tbase + c, v);
-                tmem_ld_wait();
-                const int m0 = mt * NT + c;
+            for (int p = 0; p < 2; ++p) {
+                const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + p * dstride;
+#pragma unroll 1
+                for (int c = 0; c < nh; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tbase + c, v);
+                    tmem_ld_wait();
+                    const int m0 = mt * nt + p * nh + c;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int m = m0 + j;
-                    if (m < g.M && n < g.N) {
-                        float x = __uint_as_float(v[j]);
-                        if (g.row_scale) x *= __ldg(g.row_scale + m);
-                        if (OUT == RKB_OUT_F32)
-                            static_cast<float *>(g.C)[static_cast<long>(m) * g.ldc + n] = x;
-                        else
-                            static_cast<__half *>(g.C)[static_cast<long>(m) * g.ldc + n] = __float2half_rn(x);
+                    for (int j = 0; j < 32; ++j) {
+                        const int m = m0 + j;
+                        if (c + j < nh && m < g.M && n < g.N) {
+                            float x = __uint_as_float(v[j]);
+                            if (g.row_scale) x *= __ldg(g.row_scale + m);
+                            if (OUT == RKB_OUT_F32)
+                                static_cast<float *>(g.C)[static_cast<long>(m) * g.ldc + n] = x;
+                            else
+                                static_cast<__half *>(g.C)[static_cast<long>(m) * g.ldc + n] = __float2half_rn(x);
+                        }
                     }
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty_bar(b));
+            if (lane == 0) mbar_arrive(tempty_bar);
         }
     } else {
         // dequantisers: warp (q, h): TMEM lanes 32q..+31 = weight rows, K half h
@@ -302,7 +315,7 @@ wgemm_ts_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
                     deq4_i8(u1.x, s2, o + 8);  deq4_i8(u1.y, s2, o + 10);
                     deq4_i8(u1.z, s2, o + 12); deq4_i8(u1.w, s2, o + 14);
                 }
-                tmem_st16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + A_COL0 + a * ACOLS + h * 16, o);
+                tmem_st16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acol(a) + h * 16, o);
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
@@ -321,6 +334,24 @@ wgemm_ts_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
     }
 }
 
+// Tokens per MMA nh (a tile is 2 * nh tokens): the multiple of 16 (<= 192)
+// that minimises waves x (2 * nh + 32) over the SMs; small M takes the least
+// nh that covers it.
+inline int pick_nh(int M, int n_tiles, int sms) {
+    if (M <= 2 * NH_MAX) {
+        const int nh = ((M + 1) / 2 + 15) / 16 * 16;
+        return nh < 16 ? 16 : nh;
+    }
+    int best = NH_MAX;
+    double best_t = 1e300;
+    for (int nh = NH_MAX; nh >= 96; nh -= 16) {
+        const double tiles = std::ceil(M / double(2 * nh)) * n_tiles;
+        const double t = std::ceil(tiles / sms) * (2 * nh + 32);
+        if (t < best_t * 0.999) { best_t = t; best = nh; }
+    }
+    return best;
+}
+
 template <int WBITS, int OUT>
 int launch(const rkb_wgemm_desc *d, int *err, cudaStream_t stream) {
     using C = Cfg<WBITS>;
@@ -330,13 +361,15 @@ int launch(const rkb_wgemm_desc *d, int *err, cudaStream_t stream) {
     std::call_once(attr_once[dev & 15], [] {
         cudaFuncSetAttribute(wgemm_ts_kernel<WBITS, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     });
-    CUtensorMap tb;
-    if (make_tmap_2d(&tb, d->A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, d->K, d->M, d->lda, 64, NT))
-        return ROCKET_E_SHAPE;
+    const int sms = rkb_device_sm_count(dev);
     Args g;
     g.M = d->M; g.N = d->N; g.K = d->K;
-    g.m_tiles = (d->M + NT - 1) / NT;
     g.n_tiles = (d->N + WM - 1) / WM;
+    g.nh = pick_nh(d->M, g.n_tiles, sms);
+    g.m_tiles = (d->M + 2 * g.nh - 1) / (2 * g.nh);
+    CUtensorMap tb;
+    if (make_tmap_2d(&tb, d->A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, d->K, d->M, d->lda, 64, g.nh))
+        return ROCKET_E_SHAPE;
     const int kp = (d->K + 127) / 128 * 128;
     g.kb64_total = kp / 64;
     g.k_blocks = kp / 64;
@@ -346,7 +379,6 @@ int launch(const rkb_wgemm_desc *d, int *err, cudaStream_t stream) {
     g.row_scale = d->row_scale;
     g.err = err;
     const int tiles = g.m_tiles * g.n_tiles;
-    const int sms = rkb_device_sm_count(dev);
     const int grid = tiles < sms ? tiles : sms;
     wgemm_ts_kernel<WBITS, OUT><<<grid, NUM_THREADS, C::SMEM, stream>>>(tb, g);
     cudaError_t e = cudaGetLastError();
