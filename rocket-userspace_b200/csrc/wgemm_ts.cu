@@ -268,16 +268,30 @@ wgemm_ts_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
                     tmem_ld32(tbase + c, v);
                     tmem_ld_wait();
                     const int m0 = mt * nt + p * nh + c;
+                    // the chunk's 32 token scales: lane j loads token m0 + j, then broadcast
+                    const int mj = m0 + lane;
+                    const float rs_l = (g.row_scale && mj < g.M && c + lane < nh) ? __ldg(g.row_scale + mj) : 1.0f;
+                    const bool full = c + 32 <= nh && m0 + 32 <= g.M && n < g.N;
+                    if (full) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int m = m0 + j;
-                        if (c + j < nh && m < g.M && n < g.N) {
-                            float x = __uint_as_float(v[j]);
-                            if (g.row_scale) x *= __ldg(g.row_scale + m);
-                            if (OUT == RKB_OUT_F32)
-                                static_cast<float *>(g.C)[static_cast<long>(m) * g.ldc + n] = x;
-                            else
-                                static_cast<__half *>(g.C)[static_cast<long>(m) * g.ldc + n] = __float2half_rn(x);
+                        for (int j = 0; j < 32; ++j) {
+                            const float x = __uint_as_float(v[j]) * __shfl_sync(0xffffffffu, rs_l, j);
+                            const long off = static_cast<long>(m0 + j) * g.ldc + n;
+                            if (OUT == RKB_OUT_F32) static_cast<float *>(g.C)[off] = x;
+                            else static_cast<__half *>(g.C)[off] = __float2half_rn(x);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float sj = __shfl_sync(0xffffffffu, rs_l, j);
+                            const int m = m0 + j;
+                            if (c + j < nh && m < g.M && n < g.N) {
+                                const float x = __uint_as_float(v[j]) * sj;
+                                if (OUT == RKB_OUT_F32)
+                                    static_cast<float *>(g.C)[static_cast<long>(m) * g.ldc + n] = x;
+                                else
+                                    static_cast<__half *>(g.C)[static_cast<long>(m) * g.ldc + n] = __float2half_rn(x);
+                            }
                         }
                     }
                 }
