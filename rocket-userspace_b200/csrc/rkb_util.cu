@@ -51,44 +51,67 @@ __global__ void pack_codes_i4(const int8_t *__restrict__ src, int N, int K, int 
     }
 }
 
+// Tiled fp16 scales [ntile][kblock64][256 rows][2 halves]: one thread per
+// weight row of a 256-row tile, 16 K-blocks per block; both halves of a
+// K-block go out as one coalesced 32-bit word.  bs == nullptr writes 1.0.
 __global__ void pack_scales(const float *__restrict__ bs, int N, int K, int group, int nkb,
-                            __half *__restrict__ dst, size_t total) {
+                            uint32_t *__restrict__ dst) {
+    const int r = threadIdx.x;                 // blockDim.x == TILE_N
+    const int nt = blockIdx.y;
+    const int n = nt * TILE_N + r;
     const int nG = K / group;
-    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const int h = static_cast<int>(i & 1);
-        const int r = static_cast<int>((i >> 1) & 255);
-        const size_t blk = i >> 9;
-        const int kb = static_cast<int>(blk % nkb);
-        const int nt = static_cast<int>(blk / nkb);
-        const int n = nt * TILE_N + r, k = kb * 64 + h * 32;
-        float s = 0.0f;
-        if (bs == nullptr) s = 1.0f;
-        else if (n < N && k < K) s = bs[static_cast<size_t>(n) * nG + k / group];
-        dst[i] = __float2half_rn(s);
+    const int kb0 = blockIdx.x * 16;
+    const int kb1 = kb0 + 16 < nkb ? kb0 + 16 : nkb;
+    for (int kb = kb0; kb < kb1; ++kb) {
+        float s0 = 1.0f, s1 = 1.0f;
+        if (bs) {
+            const int k0 = kb * 64, k1 = kb * 64 + 32;
+            s0 = (n < N && k0 < K) ? bs[static_cast<size_t>(n) * nG + k0 / group] : 0.0f;
+            s1 = (n < N && k1 < K) ? bs[static_cast<size_t>(n) * nG + k1 / group] : 0.0f;
+        }
+        __half2 h = __floats2half2_rn(s0, s1);
+        dst[(static_cast<size_t>(nt) * nkb + kb) * TILE_N + r] = *reinterpret_cast<uint32_t *>(&h);
     }
 }
 
+// A16[m, k] = A[m, k] * a_scale[m, k / group] (or A[m, k] when as == nullptr).
+// Grid (ceil(K / 4096), rows); 16 elements per thread.  K % 16 == 0.  VEC: A
+// and dst 16-byte aligned (vector loads / stores), else byte loads.
+template <bool VEC>
 __global__ void prescale_a(const int8_t *__restrict__ A, const float *__restrict__ as, int M,
                            int K, int group, __half *__restrict__ dst) {
-    // 8 elements per thread (K % 32 == 0 so rows split evenly)
-    const size_t total8 = static_cast<size_t>(M) * K / 8;
+    const int k = (blockIdx.x * blockDim.x + threadIdx.x) * 16;
+    if (k >= K) return;
     const int nG = as ? K / group : 0;
-    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total8;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const size_t e = i * 8;
-        const int m = static_cast<int>(e / K), k = static_cast<int>(e % K);
-        const uint2 w = *reinterpret_cast<const uint2 *>(A + e);
-        const float s = as ? as[static_cast<size_t>(m) * nG + k / group] : 1.0f;
-        const int8_t *b = reinterpret_cast<const int8_t *>(&w);
-        uint32_t o[4];
+    for (int m = blockIdx.y; m < M; m += gridDim.y) {
+        const size_t e = static_cast<size_t>(m) * K + k;
+        int8_t b[16];
+        if (VEC) {
+            *reinterpret_cast<uint4 *>(b) = *reinterpret_cast<const uint4 *>(A + e);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            __half2 p = __floats2half2_rn(static_cast<float>(b[2 * j]) * s,
-                                          static_cast<float>(b[2 * j + 1]) * s);
+            for (int j = 0; j < 16; ++j) b[j] = A[e + j];
+        }
+        const float *srow = as ? as + static_cast<size_t>(m) * nG : nullptr;
+        const bool one = (group % 16) == 0;   // all 16 elements in one group
+        const float s_all = srow ? srow[k / group] : 1.0f;
+        uint32_t o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float s0 = (srow && !one) ? srow[(k + 2 * j) / group] : s_all;
+            const float s1 = (srow && !one) ? srow[(k + 2 * j + 1) / group] : s_all;
+            __half2 p = __floats2half2_rn(static_cast<float>(b[2 * j]) * s0, static_cast<float>(b[2 * j + 1]) * s1);
             o[j] = *reinterpret_cast<uint32_t *>(&p);
         }
-        *reinterpret_cast<uint4 *>(dst + e) = make_uint4(o[0], o[1], o[2], o[3]);
+        if (VEC) {
+            uint4 *d = reinterpret_cast<uint4 *>(dst + e);
+            d[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            d[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        } else {
+            uint32_t *d = reinterpret_cast<uint32_t *>(dst + e);   // dst 4-byte aligned, K even
+#pragma unroll
+            for (int j = 0; j < 8; ++j) d[j] = o[j];
+        }
     }
 }
 
@@ -135,9 +158,10 @@ int rkb_wpack_codes(const int8_t *src, int N, int K, int bits, void *dst, cudaSt
 
 int rkb_wpack_scales(const float *b_scale, int N, int K, int group, void *dst, cudaStream_t s) {
     const int nkb = (K + 127) / 128 * 2;
-    const size_t total = rkb_wpack_scales_bytes(N, K) / sizeof(__half);
-    pack_scales<<<grid_for(total, 256), 256, 0, s>>>(b_scale, N, K, group, nkb,
-                                                      static_cast<__half *>(dst), total);
+    const int ntiles = (N + TILE_N - 1) / TILE_N;
+    if (ntiles > 65535) return ROCKET_E_SHAPE;
+    pack_scales<<<dim3((nkb + 15) / 16, ntiles), TILE_N, 0, s>>>(b_scale, N, K, group, nkb,
+                                                                 static_cast<uint32_t *>(dst));
     return status(cudaGetLastError());
 }
 
@@ -147,9 +171,15 @@ int rkb_wpack_unit_scales(int N, int K, void *dst, cudaStream_t s) {
 
 int rkb_prescale_a(const int8_t *A, const float *a_scale, int M, int K, int group, void *dst,
                    cudaStream_t s) {
-    if (K % 8) return ROCKET_E_SHAPE;
-    const size_t total8 = static_cast<size_t>(M) * K / 8;
-    prescale_a<<<grid_for(total8, 256), 256, 0, s>>>(A, a_scale, M, K, group, static_cast<__half *>(dst));
+    if (K % 16 || M <= 0) return ROCKET_E_SHAPE;
+    const int gx = (K / 16 + 255) / 256;
+    const int gy = M < 65535 ? M : 65535;
+    if (((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0)
+        prescale_a<true><<<dim3(gx, gy), 256, 0, s>>>(A, a_scale, M, K, group, static_cast<__half *>(dst));
+    else if ((reinterpret_cast<uintptr_t>(dst) & 3) == 0)
+        prescale_a<false><<<dim3(gx, gy), 256, 0, s>>>(A, a_scale, M, K, group, static_cast<__half *>(dst));
+    else
+        return ROCKET_E_SHAPE;
     return status(cudaGetLastError());
 }
 
