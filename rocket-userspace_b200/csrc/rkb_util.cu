@@ -254,3 +254,30 @@ extern "C" int rkb_int16_combine(const int32_t *hh, const int32_t *hl, const int
     int16_combine<<<grid_for(n, 256), 256, 0, s>>>(hh, hl, lh, ll, n, out);
     return status(cudaGetLastError());
 }
+
+// ---- concatenation of three device arrays (the encoder's fused q/k/v weights) ----
+namespace {
+__global__ void concat3(const uint4 *__restrict__ a, const uint4 *__restrict__ b, const uint4 *__restrict__ c,
+                        size_t n16, uint4 *__restrict__ dst) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < 3 * n16;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t part = i / n16, j = i - part * n16;
+        const uint4 *src = part == 0 ? a : part == 1 ? b : c;
+        dst[i] = src ? src[j] : make_uint4(0, 0, 0, 0);
+    }
+}
+}  // namespace
+
+// dst = [a | b | c], each `bytes` long (a multiple of 16, all pointers 16-byte
+// aligned device memory); a NULL source part is zero-filled.
+extern "C" int rkb_concat3(const void *a, const void *b, const void *c, size_t bytes, void *dst, cudaStream_t s) {
+    if (bytes % 16 || ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                        reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(dst)) & 15))
+        return ROCKET_E_SHAPE;
+    const size_t n16 = bytes / 16;
+    size_t blocks = (3 * n16 + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    concat3<<<static_cast<int>(blocks), 256, 0, s>>>(static_cast<const uint4 *>(a), static_cast<const uint4 *>(b),
+                                                      static_cast<const uint4 *>(c), n16, static_cast<uint4 *>(dst));
+    return cudaGetLastError() == cudaSuccess ? 0 : ROCKET_E_DEVICE;
+}

@@ -122,6 +122,9 @@ int rkb_cumsum_rows(const void *x, int M, int N, int exclusive, int reverse, voi
 int rkb_scale_rows(const void *x, const float *r, int M, int N, void *out, cudaStream_t s);
 int rkb_cross_entropy_rows(const void *x, const int *target, int M, int N, float *loss, cudaStream_t s);
 
+/* dst = [a | b | c] (bytes each, 16-byte multiple, aligned device pointers; NULL part -> zeros) */
+int rkb_concat3(const void *a, const void *b, const void *c, size_t bytes, void *dst, cudaStream_t s);
+
 /* ---- dtype helpers (csrc/rkb_util.cu) ---- */
 int rkb_f32_to_bf16(const void *src, size_t n, void *dst, cudaStream_t s);     /* truncating */
 int rkb_int16_split(const int16_t *src, size_t n, int8_t *hi, int8_t *lo, cudaStream_t s);
