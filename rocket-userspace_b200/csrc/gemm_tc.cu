@@ -60,7 +60,12 @@ template <> struct Kind<RKB_IN_I8> {
 
 constexpr int BM = 128;            // UMMA M (cta_group::1)
 constexpr int BK_BYTES = 128;      // one 128-byte swizzle row per K-block
-constexpr int NUM_THREADS = 192;   // 6 warps
+constexpr int NUM_THREADS = 192;   // 6 warps (single-CTA kernel)
+// CTA-pair kernel: producer, MMA and 8 epilogue warps -- two per TMEM lane
+// quarter, each draining half of the tile's columns, so epilogue-heavy GEMMs
+// (short K with bias / GELU / residual) keep up with the mainloop
+constexpr int EPI_WARPS2 = 8;
+constexpr int NUM_THREADS2 = (2 + EPI_WARPS2) * 32;
 constexpr int PREFETCH = 12;       // default K-blocks of L2 prefetch ahead of the current load
 
 template <int BN>
@@ -438,7 +443,7 @@ inline SkPlan sk_plan(int M, int N, int K, int esize, int BN, int sms) {
     if (p.L < 4) return SkPlan{};
     p.on = 1;
     p.part_bytes = static_cast<size_t>(p.R) * 2 * BM * BN * 4;
-    p.cnt_bytes = (static_cast<size_t>(p.R) * 8 * 4 + 255) & ~static_cast<size_t>(255);
+    p.cnt_bytes = (static_cast<size_t>(p.R) * 2 * EPI_WARPS2 * 4 + 255) & ~static_cast<size_t>(255);
     return p;
 }
 
@@ -525,7 +530,7 @@ int launch(const rkb_gemm_desc *d, int *err, cudaStream_t stream) {
 // coalesced 128-byte lines: word ((((r * 4 + w) * (BN / 32) + c) * 32 + j) * 32 + lane).
 struct Unit {
     int tile, k0, k1;
-    int split, slot, tl;      // stream-K: split segment, its partial slot, tail tile index
+    int split, tl;            // stream-K: split segment, tail tile index (split-K: slab index)
 };
 struct UnitIter {
     int pair, P, i, it, end;
@@ -537,7 +542,7 @@ RKB_DEV void units_begin(const Args &g, int pair, int P, UnitIter &u) {
     u.end = u.it + g.sk_L < tot ? u.it + g.sk_L : tot;
 }
 RKB_DEV bool units_next(const Args &g, int mn_tiles, UnitIter &s, Unit &u) {
-    u.split = 0; u.slot = 0; u.tl = 0;
+    u.split = 0; u.tl = 0;
     if (!g.sk) {
         const int t = s.pair + s.i * s.P;
         if (t >= mn_tiles * g.k_splits) return false;
@@ -562,7 +567,6 @@ RKB_DEV bool units_next(const Args &g, int mn_tiles, UnitIter &s, Unit &u) {
     u.tile = g.sk_W * s.P + tau;
     u.k0 = k0; u.k1 = k1;
     u.split = !(k0 == 0 && k1 == kb);
-    u.slot = 2 * s.pair + (s.it == s.pair * g.sk_L ? 0 : 1);
     u.tl = tau;
     s.it += k1 - k0;
     return true;
@@ -590,7 +594,7 @@ struct Cfg2 {
 };
 
 template <int KIND, int OUT, int BN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS2, 1)
 gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
              const __grid_constant__ CUtensorMap tmC, const Args g) {
     using C = Cfg2<BN>;
@@ -629,7 +633,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull_bar(b), 1);
-            mbar_init(tempty_bar(b), 8);   // 4 epilogue warps x 2 CTAs
+            mbar_init(tempty_bar(b), 2 * EPI_WARPS2);   // epilogue warps x 2 CTAs
         }
         mbar_init(drain_bar, 1);
         fence_mbar_init();
@@ -716,7 +720,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
             }
         }
     } else {
-        const int q = warp & 3;
+        const int e = warp - 2;                  // epilogue warp 0..7
+        const int q = warp & 3;                  // TMEM lane quarter
+        const int c_lo = (e >> 2) * (BN / 2), c_hi = c_lo + BN / 2;   // this warp's columns
         int it = 0;
         uint32_t nstore = 0;
         const uint32_t lempty0 = mapa_shared(tempty_bar(0), 0);
@@ -745,7 +751,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
                                 (static_cast<size_t>(un.tl) * 2 * BM * BN) +
                                 static_cast<size_t>(rank * 4 + q) * (BN / 32) * 1024 + lane;
 #pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
+                for (int c = c_lo; c < c_hi; c += 32) {
                     uint32_t r[32];
                     tmem_ld32(tbase + c, r);
                     tmem_ld_wait();
@@ -760,7 +766,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
                 int last = 0;
                 if (lane == 0) {
                     __threadfence();
-                    last = atomicAdd(g.sk_cnt + un.tl * 8 + rank * 4 + q, 1) == nseg - 1;
+                    last = atomicAdd(g.sk_cnt + (un.tl * 2 + rank) * EPI_WARPS2 + e, 1) == nseg - 1;
                     if (last) __threadfence();
                 }
                 last = __shfl_sync(0xffffffffu, last, 0);
@@ -781,10 +787,10 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
             if (g.tma_store) {
                 const int row0 = row - lane;
 #pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
+                for (int c = c_lo; c < c_hi; c += 32) {
                     uint32_t r[32];
                     load_chunk(r, c);
-                    if (c + 32 == BN && !from_sum) {   // accumulator drained: release it before the last store
+                    if (c + 32 == c_hi && !from_sum) {   // accumulator drained: release it before the last store
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive_cluster(b ? lempty1 : lempty0);
@@ -792,9 +798,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
                     const int col = nt * BN + c;
                     if (col >= g.N) continue;
                     pack_chunk<OUT>(g, row, col, r);
-                    // fp16 chunks are 2 KB: four buffers in the warp's 8 KB, else two
-                    constexpr int NBUF = OUT == RKB_OUT_F16 ? 4 : 2;
-                    const uint32_t buf = stg_base + q * 8192 + (nstore % NBUF) * (8192 / NBUF);
+                    // fp16 chunks are 2 KB: two buffers in the warp's 4 KB, else one
+                    constexpr int NBUF = OUT == RKB_OUT_F16 ? 2 : 1;
+                    const uint32_t buf = stg_base + e * 4096 + (nstore % NBUF) * (4096 / NBUF);
                     if (lane == 0) bulk_wait_read<NBUF - 1>();   // the store that used buf has read it
                     __syncwarp();
                     stage_store<OUT>(&tmC, buf, lane, r, col, row0, g.k_splits > 1 ? un.tl : -1);
@@ -803,7 +809,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
                 continue;
             }
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = c_lo; c < c_hi; c += 32) {
                 uint32_t r[32];
                 load_chunk(r, c);
                 const int col = nt * BN + c;
@@ -892,7 +898,7 @@ int launch2(const rkb_gemm_desc *d, int *err, cudaStream_t stream, int splits = 
             grid = 2 * sp.P;
         }
     }
-    gemm2_kernel<KIND, OUT, BN><<<grid, NUM_THREADS, C::SMEM, stream>>>(ta, tb, tc, g);
+    gemm2_kernel<KIND, OUT, BN><<<grid, NUM_THREADS2, C::SMEM, stream>>>(ta, tb, tc, g);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         fprintf(stderr, "rkb gemm2 launch: %s\n", cudaGetErrorString(e));

@@ -37,8 +37,9 @@ typedef struct {
     int act;                   /* RKB_ACT_* */
     const void *residual;      /* fp16, or NULL */
     long ldr;
-    /* split-K workspace (fp32), sized by rkb_gemm_workspace_bytes; may be NULL
-     * when that returns 0 */
+    /* workspace sized by rkb_gemm_workspace_bytes: fp32 split-K slabs, or the
+     * int8 stream-K tail's sum buffers and counters; may be NULL when that
+     * returns 0 (the kernel then runs without either) */
     void *workspace;
 } rkb_gemm_desc;
 
