@@ -543,13 +543,34 @@ def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "
         for _ in range(3):
             assert run4() == 0
         torch.cuda.synchronize()
-        # device time per block (each call waits for its own completion), no profiler events
+        # device time per block: device-resident operands, calls enqueued back to
+        # back (rocket_b200_set_async), no profiler events
+        L.rocket_b200_set_async(1)
         a.record(stream)
         for _ in range(10):
             run4()
         b.record(stream)
+        assert L.rocket_b200_sync(dev.fd) == 0
+        L.rocket_b200_set_async(0)
         torch.cuda.synchronize()
         ms4 = a.elapsed_time(b) / 10
+        # LayerNorm alone, HBM roofline: [100000, 512] fp16 (205 MB moved per call > 126 MB L2)
+        LN_ROWS = 100000
+        xl = torch.randn((LN_ROWS, d), device="cuda", generator=gq).half()
+        yl = torch.empty_like(xl)
+        runln = lambda: L.rocket_layernorm_fp16(dev.fd, LN_ROWS, d, xl.data_ptr(), pw["ln1_g"].data_ptr(),
+                                                pw["ln1_b"].data_ptr(), 1e-5, yl.data_ptr())
+        for _ in range(3):
+            assert runln() == 0
+        L.rocket_b200_set_async(1)
+        a.record(stream)
+        for _ in range(200):
+            runln()
+        b.record(stream)
+        assert L.rocket_b200_sync(dev.fd) == 0
+        L.rocket_b200_set_async(0)
+        torch.cuda.synchronize()
+        ms_ln_call = a.elapsed_time(b) / 200
         # kernel durations: a separate profiled pass
         L.rocket_b200_profile_reset()
         L.rocket_b200_profile_enable(1)
@@ -559,13 +580,15 @@ def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "
         L.rocket_b200_profile_enable(0)
         prof = rkb.profile_snapshot()
         n_ln, ms_ln = prof.get("norm", (1, 0.0))
-        ln_bytes = 2.0 * BT * d * 2 + 2 * d * 2
+        ln_bytes = 2.0 * LN_ROWS * d * 2 + 2 * d * 2
         n_at, ms_at = prof.get("attention", (1, 0.0))
         at_flops = 2 * 2.0 * nb * nh * T * T * (d // nh)
         out["config4_encoder_block"] = {
             "tflops": flops4 / ms4 / 1e9, "ms": ms4, "gflop": flops4 / 1e9,
-            "layernorm_gbs": ln_bytes / (ms_ln / max(n_ln, 1) / 1e3) / 1e9,
-            "layernorm_frac_of_measured_hbm": ln_bytes / (ms_ln / max(n_ln, 1) / 1e3) / 1e9 / peaks["hbm_gbs"],
+            "layernorm_gbs": ln_bytes / (ms_ln_call / 1e3) / 1e9,
+            "layernorm_frac_of_measured_hbm": ln_bytes / (ms_ln_call / 1e3) / 1e9 / peaks["hbm_gbs"],
+            "layernorm_us": ms_ln_call * 1e3,
+            "layernorm_note": "rocket_layernorm_fp16 on a [100000, 512] fp16 tensor (read + write 205 MB > L2), 200 calls enqueued back to back, device pointers, no profiler",
             "attention_tflops": at_flops / (ms_at / max(n_at, 1) / 1e3) / 1e12,
             "per_kernel_ms": {k: v[1] / 10 for k, v in prof.items() if v[0]},
             "note": "batched over 4 sequences via rocket_b200_encoder_block_batched_fp16"}

@@ -112,6 +112,7 @@ typedef struct {
     rkb_handle *h;
     const char *who;
     void *tmp[RKB_CALL_MAX_TMP];
+    int host_in;               /* an input was staged from host memory */
     int ntmp;
     int rc;
     struct { void *user; const void *dev; size_t bytes; } outs[4];

@@ -244,6 +244,8 @@ static void enc_stage_qkv(rkb_call *c, int d, const void *Wq, const void *Wk, co
         *bqkv = db;
         return;
     }
+    for (int i = 0; i < 3; i++)
+        if (rkb_ptr_device(ws[i]) < 0 || (bs[i] && rkb_ptr_device(bs[i]) < 0)) c->host_in = 1;
     for (int i = 0; i < 3 && !c->rc; i++) {
         if (cudaMemcpyAsync(dw + i * w, ws[i], w, cudaMemcpyDefault, c->h->stream) != cudaSuccess) {
             cudaGetLastError();

@@ -42,6 +42,7 @@ static int fa_run(int fd, int T, int n_kv, int dh, int dv, int nh, int nkvh, flo
         dV = rkb_call_in(&c, V, (size_t)nkvh * dv * n_kv * 2);
     } else {
         void *t = rkb_call_tmp(&c, (size_t)nkvh * dv * ldv * 2);
+        if (rkb_ptr_device(V) < 0) c.host_in = 1;
         if (t && cudaMemcpy2DAsync(t, (size_t)ldv * 2, V, (size_t)n_kv * 2, (size_t)n_kv * 2,
                                    (size_t)nkvh * dv, cudaMemcpyDefault, c.h->stream) != cudaSuccess) {
             cudaGetLastError();

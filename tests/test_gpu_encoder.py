@@ -201,3 +201,28 @@ def test_encoder_batched_equals_per_sequence(rkb, dev, orc):
         assert np.array_equal(yi.view(np.uint16), yb[i * T:(i + 1) * T].view(np.uint16))
         if i == 0:
             check(orc, yi, orc.encoder_block(xs[:T], p, nh, 1e-5))
+
+
+def test_async_enqueue_with_device_operands(rkb, dev, orc, gi):
+    """rocket_b200_set_async: with device inputs and outputs the encoder entries
+    return after the launches; rocket_b200_sync collects the status."""
+    import torch
+    x, g, b = (torch.from_numpy(gi[k]).cuda() for k in ("ln_x", "ln_g", "ln_b"))
+    y = torch.zeros_like(x)
+    p = gi["enc"]
+    T, d = p["x"].shape
+    pe = {k: torch.from_numpy(np.ascontiguousarray(p[k])).cuda() for k in ["x"] + list(rkb.ENCODER_KEYS)}
+    ye = torch.zeros((T, d), dtype=torch.float16, device="cuda")
+    rkb.lib.rocket_b200_set_async(1)
+    try:
+        for _ in range(3):
+            assert rkb.lib.rocket_layernorm_fp16(dev.fd, x.shape[0], x.shape[1], x.data_ptr(), g.data_ptr(),
+                                                 b.data_ptr(), 1e-5, y.data_ptr()) == 0
+            assert rkb.lib.rocket_encoder_block_fp16(dev.fd, T, d, 4, 1024, pe["x"].data_ptr(),
+                                                     *[pe[k].data_ptr() for k in rkb.ENCODER_KEYS], 1e-5,
+                                                     ye.data_ptr()) == 0
+        assert rkb.lib.rocket_b200_sync(dev.fd) == 0
+    finally:
+        rkb.lib.rocket_b200_set_async(0)
+    check(orc, y.cpu().numpy(), GOLD["ln_y"])
+    check(orc, ye.cpu().numpy(), GOLD["enc_y"])
