@@ -367,7 +367,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
             const int b = it & 1;
             const uint32_t aph = (it >> 1) & 1;
-            if (!mbar_wait(tfull_bar(b), aph, g.err, ERR_WAIT_EPILOGUE)) break;
+            if (!mbar_wait_warp(tfull_bar(b), aph, g.err, ERR_WAIT_EPILOGUE)) break;
             tc_fence_after();
             const int mt = t % g.m_tiles, nt = t / g.m_tiles;
             const int row = mt * BM + q * 32 + lane;
@@ -733,7 +733,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
         for (; units_next(g, mn_tiles, ui, un); ++it) {
             const int b = it & 1;
             const uint32_t aph = (it >> 1) & 1;
-            if (!mbar_wait(tfull_bar(b), aph, g.err, ERR_WAIT_EPILOGUE)) break;
+            if (!mbar_wait_warp(tfull_bar(b), aph, g.err, ERR_WAIT_EPILOGUE)) break;
             tc_fence_after();
             const int mt = un.tile % g.m_tiles, nt = un.tile / g.m_tiles;
             const int row = mt * 2 * BM + rank * BM + q * 32 + lane;

@@ -50,6 +50,65 @@ __device__ __forceinline__ void row_for_each(const RowView &r, int lane, F f) {
     }
 }
 
+// Rows of up to 32 * 8 * NVR halves (16-byte aligned, H % 8 == 0): one read
+// into registers, the same two-pass statistics as norm_rows (same summation
+// order, so the same results), one write.  NVR is sized to H so the register
+// footprint -- and the occupancy an HBM-bound kernel needs -- follows the row.
+template <int NVR>
+__global__ void norm_rows_reg(const __half *__restrict__ x, const __half *__restrict__ gamma,
+                              const __half *__restrict__ beta, int M, int H, float eps, int mode,
+                              __half *__restrict__ out) {
+    const int warps = blockDim.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nv = H >> 3;
+    for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(row) * H);
+        uint4 u[NVR];
+#pragma unroll
+        for (int k = 0; k < NVR; ++k)
+            if (lane + 32 * k < nv) u[k] = src[lane + 32 * k];
+        float mean = 0.f;
+        if (mode == 0) {
+            float sm = 0.f;
+#pragma unroll
+            for (int k = 0; k < NVR; ++k)
+                if (lane + 32 * k < nv) {
+                    const __half *h = reinterpret_cast<const __half *>(&u[k]);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) sm += __half2float(h[j]);
+                }
+            mean = warp_sum(sm) / H;
+        }
+        float qs = 0.f;
+#pragma unroll
+        for (int k = 0; k < NVR; ++k)
+            if (lane + 32 * k < nv) {
+                const __half *h = reinterpret_cast<const __half *>(&u[k]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) { const float dd = __half2float(h[j]) - mean; qs += dd * dd; }
+            }
+        const float rstd = rsqrtf(warp_sum(qs) / H + eps);
+        uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<size_t>(row) * H);
+#pragma unroll
+        for (int k = 0; k < NVR; ++k) {
+            const int i = lane + 32 * k;
+            if (i >= nv) continue;
+            const uint4 g = reinterpret_cast<const uint4 *>(gamma)[i];
+            const uint4 b = beta ? reinterpret_cast<const uint4 *>(beta)[i] : make_uint4(0, 0, 0, 0);
+            const __half *h = reinterpret_cast<const __half *>(&u[k]);
+            const __half *gh = reinterpret_cast<const __half *>(&g);
+            const __half *bh = reinterpret_cast<const __half *>(&b);
+            uint4 w;
+            __half *wh = reinterpret_cast<__half *>(&w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                wh[j] = __float2half_rn((__half2float(h[j]) - mean) * rstd * __half2float(gh[j]) +
+                                        __half2float(bh[j]));
+            dst[i] = w;
+        }
+    }
+}
+
 // mode 0: LayerNorm (gamma, optional beta), mode 1: RMSNorm (weight = gamma)
 __global__ void norm_rows(const __half *__restrict__ x, const __half *__restrict__ gamma,
                           const __half *__restrict__ beta, int M, int H, float eps, int mode,
@@ -319,9 +378,20 @@ int rkb_norm_rows(const void *x, const void *gamma, const void *beta, int M, int
     const int warps = 8;
     int grid = (M + warps - 1) / warps;
     if (grid > 148 * 16) grid = 148 * 16;
-    norm_rows<<<grid, warps * 32, 0, s>>>(static_cast<const __half *>(x), static_cast<const __half *>(gamma),
-                                          static_cast<const __half *>(beta), M, H, eps, rms ? 1 : 0,
-                                          static_cast<__half *>(out));
+    const bool vec = H % 8 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
+                                     reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15) == 0;
+    const __half *xh = static_cast<const __half *>(x), *gh = static_cast<const __half *>(gamma),
+                 *bh = static_cast<const __half *>(beta);
+    __half *oh = static_cast<__half *>(out);
+    const int mode = rms ? 1 : 0;
+    if (vec && H <= 512)
+        norm_rows_reg<2><<<grid, warps * 32, 0, s>>>(xh, gh, bh, M, H, eps, mode, oh);
+    else if (vec && H <= 1024)
+        norm_rows_reg<4><<<grid, warps * 32, 0, s>>>(xh, gh, bh, M, H, eps, mode, oh);
+    else if (vec && H <= 2048)
+        norm_rows_reg<8><<<grid, warps * 32, 0, s>>>(xh, gh, bh, M, H, eps, mode, oh);
+    else
+        norm_rows<<<grid, warps * 32, 0, s>>>(xh, gh, bh, M, H, eps, mode, oh);
     return status();
 }
 
