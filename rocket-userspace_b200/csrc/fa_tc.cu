@@ -91,7 +91,10 @@ __host__ __device__ inline Plan plan_for(int bkv, int dhp, int dv) {
     return p;
 }
 
-template <int BKV>
+// MASK: 0 none, 1 16-byte vector loads, 2 scalar loads; CAP: soft-cap on.
+// Separate instantiations keep the fully unrolled score loop free of the
+// branches (and the tanh code) a call does not use.
+template <int BKV, int MASK, bool CAP>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
           const __grid_constant__ CUtensorMap tmV, const Args g) {
@@ -215,34 +218,35 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
         const int t = qt * BQ + row;
         const uint32_t tl = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
         const float sc2 = g.scale;
-        const bool capped = g.softcap != 0.f;
-        const __half *mrow = (g.mask && t < g.T) ? g.mask + static_cast<size_t>(t) * g.n_kv : nullptr;
+        const __half *mrow = (MASK && t < g.T) ? g.mask + static_cast<size_t>(t) * g.n_kv : nullptr;
         float m = -INFINITY, l = 0.f;
         uint8_t *prow = smem + pl.p + row * 128;
         bool ok = true;
         for (int j = 0; j < nkb; ++j) {
             const int kbase = j * BKV;
             // this block's mask values, fetched before the scores arrive
-            uint32_t mk[BKV / 2];
-            if (mrow) {
-                if (g.mask_vec) {
+            uint32_t mk[MASK ? BKV / 2 : 1];
+            if (MASK) {
+                if (mrow) {
+                    if (MASK == 1) {
 #pragma unroll
-                    for (int c = 0; c < BKV; c += 8) {
-                        uint4 v = make_uint4(0, 0, 0, 0);
-                        if (kbase + c < g.n_kv) v = __ldg(reinterpret_cast<const uint4 *>(mrow + kbase + c));
-                        mk[c / 2] = v.x; mk[c / 2 + 1] = v.y; mk[c / 2 + 2] = v.z; mk[c / 2 + 3] = v.w;
+                        for (int c = 0; c < BKV; c += 8) {
+                            uint4 v = make_uint4(0, 0, 0, 0);
+                            if (kbase + c < g.n_kv) v = __ldg(reinterpret_cast<const uint4 *>(mrow + kbase + c));
+                            mk[c / 2] = v.x; mk[c / 2 + 1] = v.y; mk[c / 2 + 2] = v.z; mk[c / 2 + 3] = v.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < BKV; c += 2) {
+                            const unsigned short lo = kbase + c < g.n_kv ? __ldg(reinterpret_cast<const unsigned short *>(mrow + kbase + c)) : 0;
+                            const unsigned short hi = kbase + c + 1 < g.n_kv ? __ldg(reinterpret_cast<const unsigned short *>(mrow + kbase + c + 1)) : 0;
+                            mk[c / 2] = lo | (static_cast<uint32_t>(hi) << 16);
+                        }
                     }
                 } else {
 #pragma unroll
-                    for (int c = 0; c < BKV; c += 2) {
-                        const unsigned short lo = kbase + c < g.n_kv ? __ldg(reinterpret_cast<const unsigned short *>(mrow + kbase + c)) : 0;
-                        const unsigned short hi = kbase + c + 1 < g.n_kv ? __ldg(reinterpret_cast<const unsigned short *>(mrow + kbase + c + 1)) : 0;
-                        mk[c / 2] = lo | (static_cast<uint32_t>(hi) << 16);
-                    }
+                    for (int c = 0; c < BKV / 2; ++c) mk[c] = 0;
                 }
-            } else {
-#pragma unroll
-                for (int c = 0; c < BKV / 2; ++c) mk[c] = 0;
             }
             if (!mbar_wait_warp(s_full, j & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
             tc_fence_after();
@@ -260,14 +264,17 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             if (lane == 0) mbar_arrive(s_free);
             // the reference's score (fa_score), then into the log2 domain
             float mx = -INFINITY;
+            const int nvalid = g.n_kv - kbase;   // keys of this block that exist
 #pragma unroll
             for (int c = 0; c < BKV; ++c) {
                 float s = sv[c] * sc2;
-                if (capped) s = g.softcap * tanhf(s / g.softcap);
-                const __half2 mm = *reinterpret_cast<const __half2 *>(&mk[c / 2]);
-                s += (c & 1) ? __high2float(mm) : __low2float(mm);
+                if (CAP) s = g.softcap * tanhf(s / g.softcap);
+                if (MASK) {
+                    const __half2 mm = *reinterpret_cast<const __half2 *>(&mk[c / 2]);
+                    s += (c & 1) ? __high2float(mm) : __low2float(mm);
+                }
                 s = fmaxf(s, -30000.f);
-                s = (kbase + c < g.n_kv) ? s * LOG2E : -INFINITY;
+                s = (c < nvalid) ? s * LOG2E : -INFINITY;
                 sv[c] = s;
                 mx = fmaxf(mx, s);
             }
@@ -352,7 +359,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
     }
 }
 
-template <int BKV>
+template <int BKV, int MASK, bool CAP>
 int launch(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, const Args &g,
            cudaStream_t stream) {
     const Plan pl = plan_for(BKV, g.dhp, g.dv);
@@ -360,14 +367,29 @@ int launch(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, 
     int dev = 0;
     cudaGetDevice(&dev);
     std::call_once(once[dev & 15], [] {
-        cudaFuncSetAttribute(fa_kernel<BKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaFuncSetAttribute(fa_kernel<BKV, MASK, CAP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     });
     // BKV 64 allocates all 512 TMEM columns: ask for more than half the SM's
     // shared memory so a second CTA never lands on the SM and stalls in alloc
     const int smem = BKV == 64 && pl.total < 116 * 1024 ? 116 * 1024 : pl.total;
     dim3 grid((g.T + BQ - 1) / BQ, static_cast<unsigned>(g.n_head));
-    fa_kernel<BKV><<<grid, NUM_THREADS, smem, stream>>>(tq, tk, tv, g);
+    fa_kernel<BKV, MASK, CAP><<<grid, NUM_THREADS, smem, stream>>>(tq, tk, tv, g);
     return 0;
+}
+
+template <int BKV>
+int launch_kind(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, const Args &g,
+                cudaStream_t stream) {
+    const int mask = g.mask ? (g.mask_vec ? 1 : 2) : 0;
+    const bool cap = g.softcap != 0.f;
+    switch (mask * 2 + (cap ? 1 : 0)) {
+    case 0: return launch<BKV, 0, false>(tq, tk, tv, g, stream);
+    case 1: return launch<BKV, 0, true>(tq, tk, tv, g, stream);
+    case 2: return launch<BKV, 1, false>(tq, tk, tv, g, stream);
+    case 3: return launch<BKV, 1, true>(tq, tk, tv, g, stream);
+    case 4: return launch<BKV, 2, false>(tq, tk, tv, g, stream);
+    default: return launch<BKV, 2, true>(tq, tk, tv, g, stream);
+    }
 }
 
 }  // namespace fa
@@ -405,8 +427,8 @@ extern "C" int rkb_flash_attn_ex(const void *Q, const void *K, const void *V, lo
     g.mask_vec = mask && (n_kv % 8 == 0) && ((reinterpret_cast<uintptr_t>(mask) & 15) == 0);
     g.out = static_cast<__half *>(out);
     g.err = err;
-    if (bkv == 128) launch<128>(tq, tk, tv, g, stream);
-    else launch<64>(tq, tk, tv, g, stream);
+    if (bkv == 128) launch_kind<128>(tq, tk, tv, g, stream);
+    else launch_kind<64>(tq, tk, tv, g, stream);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         fprintf(stderr, "rkb flash attention launch: %s\n", cudaGetErrorString(e));
