@@ -283,7 +283,9 @@ static void enc_mha_core(rkb_call *c, int nb, int T, int d, int n_head, const vo
     /* head_dim 64: the register-resident-O kernel; other head dims: the flash
      * kernel over the same split heads (nb * n_head heads of Tp rows, output
      * interleaved back into ctx[token][head * dh]) */
-    if (!c->rc && dh == 64)
+    static int force_fa = -1;
+    if (force_fa < 0) force_fa = (int)rkb_env_long("ROCKET_ATTN_FA", 0);
+    if (!c->rc && dh == 64 && !force_fa)
         rkb_call_check(c, rkb_attention(Q, K, Vt, nb, n_head, T, Tp, dh, 1.0f / sqrtf((float)dh), ctx, d,
                                    c->h->err_dev, c->h->stream));
     else if (!c->rc)
