@@ -365,7 +365,7 @@ def main_ours(args):
     others = None
     if world == 1 and not args.no_extra:
         others = other_configs(rkb, torch, peaks, derived_peak,
-                               tuple(args.side.split(",")) if args.side else ("c1", "c2", "c3", "c4"))
+                               tuple(args.side.split(",")) if args.side else ("c1", "c2", "c3", "c4", "fa"))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -393,7 +393,7 @@ def main_ours(args):
     return 0
 
 
-def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "c4")):
+def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "c4", "fa")):
     """fp16 (config 2), W4A8 group-wise (config 3) and int8 latency (config 1)."""
     L = rkb.lib
     out = {}
@@ -593,6 +593,30 @@ def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "
             "per_kernel_ms": {k: v[1] / 10 for k, v in prof.items() if v[0]},
             "note": "batched over 4 sequences via rocket_b200_encoder_block_batched_fp16"}
 
+    # masked grouped-query flash attention (rocket_flash_attn_fp16), Llama-style prefill shapes
+    if "fa" in which:
+        res = {}
+        for (T, nkv, dh, nh, nkvh, masked) in [(4096, 4096, 128, 32, 8, True), (4096, 4096, 128, 32, 8, False),
+                                              (2048, 2048, 256, 16, 8, True)]:
+            gf = torch.Generator(device="cuda")
+            gf.manual_seed(T + dh)
+            Qf = (torch.randn((nh, T, dh), device="cuda", generator=gf) * 0.5).half()
+            Kf = (torch.randn((nkvh, nkv, dh), device="cuda", generator=gf) * 0.5).half()
+            Vf = torch.randn((nkvh, dh, nkv), device="cuda", generator=gf).half()
+            Mf = None
+            if masked:
+                pos = nkv - T + torch.arange(T, device="cuda")[:, None]
+                Mf = torch.where(torch.arange(nkv, device="cuda")[None, :] <= pos, 0.0, float("-inf")).half()
+            Of = torch.empty((nh, T, dh), device="cuda", dtype=torch.float16)
+            runf = (lambda Qf=Qf, Kf=Kf, Vf=Vf, Mf=Mf, Of=Of, T=T, nkv=nkv, dh=dh, nh=nh, nkvh=nkvh:
+                    L.rocket_flash_attn_fp16(dev.fd, T, nkv, dh, dh, nh, nkvh, dh ** -0.5, 0.0, Qf.data_ptr(),
+                                             Kf.data_ptr(), Vf.data_ptr(),
+                                             Mf.data_ptr() if Mf is not None else None, Of.data_ptr()))
+            msf = timed(runf, 10)
+            res[f"T{T}_kv{nkv}_dh{dh}_h{nh}/{nkvh}_{'causal' if masked else 'nomask'}"] = {
+                "us": msf * 1e3, "tflops_all_scores": 4.0 * T * nkv * dh * nh / msf / 1e9}
+        out["flash_attn_gqa"] = res
+
     # config 1: int8 64x512x256 one-shot (latency)
     if "c1" in which:
         import numpy as np
@@ -626,7 +650,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true")
-    ap.add_argument("--side", default="", help="comma list of side configs to run (c1,c2,c3,c4)")
+    ap.add_argument("--side", default="", help="comma list of side configs to run (c1,c2,c3,c4,fa)")
     ap.add_argument("--side-only", action="store_true", help="run only the side configs (profiling)")
     ap.add_argument("--layers", default="", help="comma list of GEMMs to run (profiling); default all four")
     args = ap.parse_args()
@@ -640,7 +664,7 @@ def main():
         rkb = load_pkg()
         peaks, _ = load_peaks()
         res = other_configs(rkb, torch, peaks, 2.0 * peaks.get("bf16_tflops", 1590.0),
-                            tuple(args.side.split(",")) if args.side else ("c1", "c2", "c3", "c4"))
+                            tuple(args.side.split(",")) if args.side else ("c1", "c2", "c3", "c4", "fa"))
         print(json.dumps({"side_configs": res}), flush=True)
         return 0
     return main_ours(args)
