@@ -923,7 +923,9 @@ inline std::atomic<int> &policy_sk() { static std::atomic<int> v{-1}; return v; 
 inline Pick pick_kernel(int M, int N, int K, int esize) {
     static const char *e = getenv("ROCKET_GEMM_VARIANT");
     const int kb = (K * esize + BK_BYTES - 1) / BK_BYTES;
-    const int sms = 148;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = rkb_device_sm_count(dev);
     const int pv = policy_variant().load(std::memory_order_relaxed);
     const int psk = policy_sk().load(std::memory_order_relaxed);
     if (pv || e) {
@@ -1011,7 +1013,9 @@ inline int pick_splits(const rkb_gemm_desc *d) {
         s = atoi(e);
         if (s > 4) s = 4;
     } else {
-        const int pairs = 74;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int pairs = rkb_device_sm_count(dev) / 2;
         const int tiles = ((d->M + 2 * BM - 1) / (2 * BM)) * ((d->N + 255) / 256);
         if (tiles >= pairs || kblocks < 48 || (d->N & 7)) return 1;
         s = pairs / tiles;
