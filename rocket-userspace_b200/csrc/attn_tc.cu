@@ -189,16 +189,24 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             // online softmax in the log2 domain
             const int kbase = j * BKV;
             float mx = m;
+            if (kbase + BKV <= g.T) {   // every key of the block exists: no per-key test
 #pragma unroll
-            for (int c = 0; c < BKV; ++c) {
-                sv[c] = (kbase + c < g.T) ? sv[c] * g.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, sv[c]);
+                for (int c = 0; c < BKV; ++c) {
+                    sv[c] *= g.scale_log2;
+                    mx = fmaxf(mx, sv[c]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < BKV; ++c) {
+                    sv[c] = (kbase + c < g.T) ? sv[c] * g.scale_log2 : -INFINITY;
+                    mx = fmaxf(mx, sv[c]);
+                }
             }
-            const float alpha = exp2f(m - mx);   // m = -inf on the first block -> 0
+            const float alpha = ex2_approx(m - mx);   // m = -inf on the first block -> 0
             float sum = 0.f;
 #pragma unroll
             for (int c = 0; c < BKV; ++c) {
-                sv[c] = exp2f(sv[c] - mx);
+                sv[c] = ex2_approx(sv[c] - mx);
                 sum += sv[c];
             }
             l = l * alpha + sum;

@@ -281,11 +281,11 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             // lazy rescale: keep the reference max unless this block exceeds it by 2^8
             float m_new = m;
             if (mx > m + RESCALE_LOG2) m_new = mx;
-            const float alpha = exp2f(m - m_new);   // 1 when unchanged, 0 on the first block
+            const float alpha = m_new == m ? 1.f : ex2_approx(m - m_new);   // 0 on the first block
             float sum = 0.f;
 #pragma unroll
             for (int c = 0; c < BKV; ++c) {
-                sv[c] = exp2f(sv[c] - m_new);
+                sv[c] = ex2_approx(sv[c] - m_new);
                 sum += sv[c];
             }
             l = l * alpha + sum;

@@ -42,6 +42,15 @@ RKB_DEV uint64_t global_timer_ns() {
     return t;
 }
 
+// Hardware base-2 exponential (MUFU, flush-to-zero).  Used for softmax
+// weights, whose arguments are <= 0 (score minus running max): the result is
+// in [0, 1], -inf gives 0, and the ~2 ulp error is far below fp16 resolution.
+RKB_DEV float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // ---- mbarriers -------------------------------------------------------------
 RKB_DEV void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
