@@ -3,9 +3,11 @@
  * (reference include/rocket_encoder.h:28-49; host definition
  * src/rocket_encoder.c:79-108):
  *     x = x + MHA(LN1(x));  out = x + GELU(LN2(x) W1^T + b1) W2^T + b2
- * Ten launches: LN, three q/k/v GEMMs, head split, fused attention, output
- * projection with bias + residual fused, LN, fc1 with bias + GELU fused, fc2
- * with bias + residual fused.  head_dim must be 64.
+ * Eight kernels: LN, one fused q/k/v GEMM (N = 3d), head split, fused
+ * attention, output projection with bias + residual fused, LN, fc1 with bias
+ * + GELU fused, fc2 with bias + residual fused (plus one gather of the q/k/v
+ * weights when they are device-resident).  head_dim must be a multiple of 16
+ * and at most 256.
  */
 #ifndef ROCKET_ENCODER_H
 #define ROCKET_ENCODER_H

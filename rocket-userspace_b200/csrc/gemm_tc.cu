@@ -12,7 +12,11 @@
 //               accumulator of 128 lanes x BN columns; two accumulators
 //               alternate so the epilogue of tile i overlaps the MMAs of i+1.
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (warp w owns TMEM
-//               lanes 32*(w%4)..+31 = output rows), convert, store to global.
+//               lanes 32*(w%4)..+31 = output rows), convert, store to global
+//               (directly, or staged in shared memory and written by TMA).
+// The CTA-pair kernel (gemm2_kernel, further down) computes 256-row tiles on
+// two SMs with tcgen05.mma.cta_group::2 and has 8 epilogue warps; it also
+// carries the int8 stream-K tail and the fp16 split-K slabs.
 // Both operands are K-major ("TN"), which is the layout the reference API
 // defines (B is [N,K] row-major), so no transposes are ever made.
 #include <cuda.h>
