@@ -187,26 +187,23 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             __syncwarp();
             if (lane == 0) mbar_arrive(s_free);
             // online softmax in the log2 domain
+            // the scale (> 0) is folded into the exponent: max over raw scores,
+            // weights ex2(s * scale_log2 - m); keys past T exist only in the last block
             const int kbase = j * BKV;
-            float mx = m;
-            if (kbase + BKV <= g.T) {   // every key of the block exists: no per-key test
+            if (kbase + BKV > g.T) {
 #pragma unroll
-                for (int c = 0; c < BKV; ++c) {
-                    sv[c] *= g.scale_log2;
-                    mx = fmaxf(mx, sv[c]);
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < BKV; ++c) {
-                    sv[c] = (kbase + c < g.T) ? sv[c] * g.scale_log2 : -INFINITY;
-                    mx = fmaxf(mx, sv[c]);
-                }
+                for (int c = 0; c < BKV; ++c)
+                    if (kbase + c >= g.T) sv[c] = -INFINITY;
             }
+            float mr = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < BKV; ++c) mr = fmaxf(mr, sv[c]);
+            const float mx = fmaxf(m, mr * g.scale_log2);
             const float alpha = ex2_approx(m - mx);   // m = -inf on the first block -> 0
             float sum = 0.f;
 #pragma unroll
             for (int c = 0; c < BKV; ++c) {
-                sv[c] = ex2_approx(sv[c] - mx);
+                sv[c] = ex2_approx(fmaf(sv[c], g.scale_log2, -mx));
                 sum += sv[c];
             }
             l = l * alpha + sum;
