@@ -13,10 +13,14 @@
 //               0..127), O_j = P_j V_j (M=128, N=64, TMEM cols 128..191); S_{j+1}
 //               is issued as soon as S_j has been read, so it overlaps the
 //               softmax of block j
-//   warps 2..5  softmax: each thread owns one query row: reads its 128 scores
-//               from TMEM, online max / exp2 / row-sum in fp32, writes P_j as
-//               fp16 into a 128-byte-swizzled shared tile for the P V MMA, and
-//               folds O_{j-1} from TMEM into its 64 fp32 output registers
+//   warps 2..9  softmax, two warps per TMEM lane quarter: each thread owns one
+//               query row and half of every 128-key block; the pair exchanges
+//               half-block row maxima through shared memory (an mbarrier with
+//               a bounded wait), then each computes exp2 weights and its part
+//               of the row sum in fp32, writes its 64-key panel of P_j as fp16
+//               into the 128-byte-swizzled shared tile for the P V MMA, and
+//               folds its 32 columns of O_{j-1} from TMEM into registers; the
+//               two partial row sums are added at the end
 // Keys past T (the last block) are masked to -inf.  Inputs come from
 // rkb_split_heads: Q, K [B*H, Tp, 64] and V^T [B*H, 64, Tp], zero-padded.
 #include <cuda.h>
@@ -35,7 +39,7 @@ namespace rkb {
 namespace attn {
 
 constexpr int BQ = 128, BKV = 128, DH = 64;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 320;       // producer, MMA, 8 softmax warps
 constexpr int Q_BYTES = BQ * DH * 2;        // 16 KB
 constexpr int K_BYTES = BKV * DH * 2;       // 16 KB
 constexpr int VT_BYTES = DH * BKV * 2;      // 16 KB (two 64-key panels of 8 KB)
@@ -45,8 +49,10 @@ constexpr int KV_STAGE = K_BYTES + VT_BYTES;
 constexpr int OFF_Q = 0;
 constexpr int OFF_KV = Q_BYTES;
 constexpr int OFF_P = OFF_KV + KV_STAGES * KV_STAGE;
-constexpr int OFF_BAR = OFF_P + P_BYTES;
-constexpr int NBARS = 1 + 2 * KV_STAGES + 4;
+constexpr int OFF_X = OFF_P + P_BYTES;        // row-max exchange [2 parities][2 halves][128] + sums [2][128]
+constexpr int X_BYTES = (2 * 2 * BQ + 2 * BQ) * 4;
+constexpr int OFF_BAR = OFF_X + X_BYTES;
+constexpr int NBARS = 1 + 2 * KV_STAGES + 4 + 8;
 constexpr int SMEM = OFF_BAR + NBARS * 8 + 16 + 1024;
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t S_COL = 0, O_COL = 128;
@@ -75,6 +81,10 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const uint32_t s_free = smem_u32(&bars[2 + 2 * KV_STAGES]);
     const uint32_t p_full = smem_u32(&bars[3 + 2 * KV_STAGES]);
     const uint32_t o_full = smem_u32(&bars[4 + 2 * KV_STAGES]);
+    // per TMEM lane quarter: the two softmax warps of those rows exchange their
+    // half-block row maxima (every block) and their row sums (at the end)
+    auto xmax_bar = [&](int q) { return smem_u32(&bars[5 + 2 * KV_STAGES + q]); };
+    auto xsum_bar = [&](int q) { return smem_u32(&bars[9 + 2 * KV_STAGES + q]); };
     auto sK = [&](int s) { return sb + OFF_KV + s * KV_STAGE; };
     auto sVt = [&](int s) { return sb + OFF_KV + s * KV_STAGE + K_BYTES; };
 
@@ -91,9 +101,13 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             mbar_init(kv_empty(s), 1);
         }
         mbar_init(s_full, 1);
-        mbar_init(s_free, 4);
-        mbar_init(p_full, 4);
+        mbar_init(s_free, 8);
+        mbar_init(p_full, 8);
         mbar_init(o_full, 1);
+        for (int q = 0; q < 4; ++q) {
+            mbar_init(xmax_bar(q), 64);
+            mbar_init(xsum_bar(q), 64);
+        }
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -162,23 +176,31 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             }
         }
     } else {
+        // softmax: warps 2..9; warp pair (e, e + 4) shares TMEM lane quarter q
+        // (query rows 32q..32q+31) and takes key half `half` of every block
+        const int e = warp - 2;
         const int q4 = warp & 3;
+        const int half = e >> 2;
         const int row = q4 * 32 + lane;
         const uint32_t tl = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
-        float o[DH];
+        float *xm = reinterpret_cast<float *>(smem + OFF_X);        // [parity][half][row]
+        float *xs = xm + 2 * 2 * BQ;                                // [half][row]
+        constexpr int HK = BKV / 2;                                 // keys per warp per block
+        constexpr int HD = DH / 2;                                  // output columns per warp
+        float o[HD];
 #pragma unroll
-        for (int c = 0; c < DH; ++c) o[c] = 0.f;
+        for (int c = 0; c < HD; ++c) o[c] = 0.f;
         float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-        uint8_t *prow = smem + OFF_P + row * 128;
+        uint8_t *prow = smem + OFF_P + half * (P_BYTES / 2) + row * 128;
         bool ok = true;
         for (int j = 0; j < nkb; ++j) {
             if (!mbar_wait(s_full, j & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
             tc_fence_after();
-            float sv[BKV];
+            float sv[HK];
 #pragma unroll
-            for (int c = 0; c < BKV; c += 32) {
+            for (int c = 0; c < HK; c += 32) {
                 uint32_t r[32];
-                tmem_ld32(tl + S_COL + c, r);
+                tmem_ld32(tl + S_COL + half * HK + c, r);
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 32; ++i) sv[c + i] = __uint_as_float(r[i]);
@@ -186,54 +208,53 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(s_free);
-            // online softmax in the log2 domain
             // the scale (> 0) is folded into the exponent: max over raw scores,
             // weights ex2(s * scale_log2 - m); keys past T exist only in the last block
-            const int kbase = j * BKV;
-            if (kbase + BKV > g.T) {
+            const int kbase = j * BKV + half * HK;
+            if (j * BKV + BKV > g.T) {
 #pragma unroll
-                for (int c = 0; c < BKV; ++c)
+                for (int c = 0; c < HK; ++c)
                     if (kbase + c >= g.T) sv[c] = -INFINITY;
             }
             float mr = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < BKV; ++c) mr = fmaxf(mr, sv[c]);
+            for (int c = 0; c < HK; ++c) mr = fmaxf(mr, sv[c]);
+            // exchange half-block maxima with the partner warp (bounded wait)
+            xm[((j & 1) * 2 + half) * BQ + row] = mr;
+            mbar_arrive(xmax_bar(q4));
+            if (!mbar_wait(xmax_bar(q4), j & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
+            mr = fmaxf(mr, xm[((j & 1) * 2 + (half ^ 1)) * BQ + row]);
             const float mx = fmaxf(m, mr * g.scale_log2);
             const float alpha = ex2_approx(m - mx);   // m = -inf on the first block -> 0
             float sum = 0.f;
 #pragma unroll
-            for (int c = 0; c < BKV; ++c) {
+            for (int c = 0; c < HK; ++c) {
                 sv[c] = ex2_approx(fmaf(sv[c], g.scale_log2, -mx));
                 sum += sv[c];
             }
-            l = l * alpha + sum;
+            l = l * alpha + sum;                      // this warp's half of the row sum
             m = mx;
-            // fold O_{j-1}; after this the P tile and the O columns are free
+            // fold O_{j-1} (this warp's half of the columns); then P and O are free
             if (j > 0) {
                 if (!mbar_wait(o_full, (j - 1) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
                 tc_fence_after();
+                uint32_t r[32];
+                tmem_ld32(tl + O_COL + half * HD, r);
+                tmem_ld_wait();
 #pragma unroll
-                for (int c = 0; c < DH; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(tl + O_COL + c, r);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[c + i] = o[c + i] * alpha_prev + __uint_as_float(r[i]);
-                }
+                for (int i = 0; i < HD; ++i) o[i] = o[i] * alpha_prev + __uint_as_float(r[i]);
             }
             alpha_prev = alpha;
-            // P_j as fp16 into the swizzled [128 x 128] A tile (two 64-key panels)
+            // P_j as fp16: this warp's 64 keys are panel `half` of the swizzled A tile
 #pragma unroll
-            for (int cg = 0; cg < 16; ++cg) {
-                uint32_t h[4];
+            for (int c = 0; c < 8; ++c) {
+                uint32_t hv[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    __half2 p = __floats2half2_rn(sv[cg * 8 + 2 * i], sv[cg * 8 + 2 * i + 1]);
-                    h[i] = *reinterpret_cast<uint32_t *>(&p);
+                    __half2 p = __floats2half2_rn(sv[c * 8 + 2 * i], sv[c * 8 + 2 * i + 1]);
+                    hv[i] = *reinterpret_cast<uint32_t *>(&p);
                 }
-                const int panel = cg >> 3, c = cg & 7;
-                *reinterpret_cast<uint4 *>(prow + panel * (P_BYTES / 2) + ((c ^ (row & 7)) << 4)) =
-                    make_uint4(h[0], h[1], h[2], h[3]);
+                *reinterpret_cast<uint4 *>(prow + ((c ^ (row & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
             }
             fence_proxy_async_smem();
             tc_fence_before();
@@ -242,28 +263,31 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         }
         if (ok && nkb > 0 && mbar_wait(o_full, (nkb - 1) & 1, g.err, ERR_WAIT_EPILOGUE)) {
             tc_fence_after();
+            uint32_t r[32];
+            tmem_ld32(tl + O_COL + half * HD, r);
+            tmem_ld_wait();
 #pragma unroll
-            for (int c = 0; c < DH; c += 32) {
-                uint32_t r[32];
-                tmem_ld32(tl + O_COL + c, r);
-                tmem_ld_wait();
+            for (int i = 0; i < HD; ++i) o[i] = o[i] * alpha_prev + __uint_as_float(r[i]);
+            // the row sum is the two halves' sum (a + b == b + a: both warps agree)
+            xs[half * BQ + row] = l;
+            mbar_arrive(xsum_bar(q4));
+            if (mbar_wait(xsum_bar(q4), 0, g.err, ERR_WAIT_EPILOGUE)) {
+                const float lt = l + xs[(half ^ 1) * BQ + row];
+                const int t = qt * BQ + row;
+                if (t < g.T) {
+                    const int b = bh / g.H, h = bh % g.H;
+                    __half *dst = g.out + static_cast<long>(b * g.T + t) * g.ldo + h * DH + half * HD;
+                    const float inv = 1.f / lt;
 #pragma unroll
-                for (int i = 0; i < 32; ++i) o[c + i] = o[c + i] * alpha_prev + __uint_as_float(r[i]);
-            }
-            const int t = qt * BQ + row;
-            if (t < g.T) {
-                const int b = bh / g.H, h = bh % g.H;
-                __half *dst = g.out + static_cast<long>(b * g.T + t) * g.ldo + h * DH;
-                const float inv = 1.f / l;
+                    for (int c = 0; c < HD; c += 8) {
+                        uint32_t w[4];
 #pragma unroll
-                for (int c = 0; c < DH; c += 8) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        __half2 p = __floats2half2_rn(o[c + 2 * i] * inv, o[c + 2 * i + 1] * inv);
-                        w[i] = *reinterpret_cast<uint32_t *>(&p);
+                        for (int i = 0; i < 4; ++i) {
+                            __half2 p = __floats2half2_rn(o[c + 2 * i] * inv, o[c + 2 * i + 1] * inv);
+                            w[i] = *reinterpret_cast<uint32_t *>(&p);
+                        }
+                        *reinterpret_cast<uint4 *>(dst + c) = make_uint4(w[0], w[1], w[2], w[3]);
                     }
-                    *reinterpret_cast<uint4 *>(dst + c) = make_uint4(w[0], w[1], w[2], w[3]);
                 }
             }
         }
