@@ -49,13 +49,29 @@ constexpr int KV_STAGE = K_BYTES + VT_BYTES;
 constexpr int OFF_Q = 0;
 constexpr int OFF_KV = Q_BYTES;
 constexpr int OFF_P = OFF_KV + KV_STAGES * KV_STAGE;
-constexpr int OFF_X = OFF_P + P_BYTES;        // row-max exchange [2 parities][2 halves][128] + sums [2][128]
+constexpr int P_BUFS = 2;                     // P double-buffered: softmax j+1 overlaps P_j V_j
+constexpr int OFF_X = OFF_P + P_BUFS * P_BYTES;   // row-max exchange [2 parities][2 halves][128] + sums [2][128]
 constexpr int X_BYTES = (2 * 2 * BQ + 2 * BQ) * 4;
 constexpr int OFF_BAR = OFF_X + X_BYTES;
-constexpr int NBARS = 1 + 2 * KV_STAGES + 4 + 8;
+constexpr int NBARS = 1 + 2 * KV_STAGES + 5 + 8;
+constexpr float RESCALE_LOG2 = 8.f;    // the reference max moves only when a row's max grows by > 2^8
 constexpr int SMEM = OFF_BAR + NBARS * 8 + 16 + 1024;
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t S_COL = 0, O_COL = 128;
+
+RKB_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+          "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]),
+          "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]),
+          "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+          "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+RKB_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 struct Args {
     int T, Tp, H, nkb;
@@ -80,11 +96,13 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const uint32_t s_full = smem_u32(&bars[1 + 2 * KV_STAGES]);
     const uint32_t s_free = smem_u32(&bars[2 + 2 * KV_STAGES]);
     const uint32_t p_full = smem_u32(&bars[3 + 2 * KV_STAGES]);
-    const uint32_t o_full = smem_u32(&bars[4 + 2 * KV_STAGES]);
+    // P_j V_j done (it read P buffer j & 1 and accumulated into O): completion k
+    // of pv_done(b) is block b + 2k, so block j waits parity (j >> 1) & 1
+    auto pv_done = [&](int b) { return smem_u32(&bars[4 + 2 * KV_STAGES + b]); };
     // per TMEM lane quarter: the two softmax warps of those rows exchange their
     // half-block row maxima (every block) and their row sums (at the end)
-    auto xmax_bar = [&](int q) { return smem_u32(&bars[5 + 2 * KV_STAGES + q]); };
-    auto xsum_bar = [&](int q) { return smem_u32(&bars[9 + 2 * KV_STAGES + q]); };
+    auto xmax_bar = [&](int q) { return smem_u32(&bars[6 + 2 * KV_STAGES + q]); };
+    auto xsum_bar = [&](int q) { return smem_u32(&bars[10 + 2 * KV_STAGES + q]); };
     auto sK = [&](int s) { return sb + OFF_KV + s * KV_STAGE; };
     auto sVt = [&](int s) { return sb + OFF_KV + s * KV_STAGE + K_BYTES; };
 
@@ -103,7 +121,8 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         mbar_init(s_full, 1);
         mbar_init(s_free, 8);
         mbar_init(p_full, 8);
-        mbar_init(o_full, 1);
+        mbar_init(pv_done(0), 1);
+        mbar_init(pv_done(1), 1);
         for (int q = 0; q < 4; ++q) {
             mbar_init(xmax_bar(q), 64);
             mbar_init(xsum_bar(q), 64);
@@ -161,13 +180,14 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                 if (!mbar_wait(p_full, j & 1, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
                 tc_fence_after();
                 const int s = j % KV_STAGES;
+                const uint32_t pbuf = sb + OFF_P + (j & 1) * P_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t pd = smem_desc_sw128(sb + OFF_P + (kk >> 2) * (P_BYTES / 2) + (kk & 3) * 32);
+                    const uint64_t pd = smem_desc_sw128(pbuf + (kk >> 2) * (P_BYTES / 2) + (kk & 3) * 32);
                     const uint64_t vd = smem_desc_sw128(sVt(s) + (kk >> 2) * (VT_BYTES / 2) + (kk & 3) * 32);
-                    tc_mma_f16(tmem + O_COL, pd, vd, IDO, kk > 0);
+                    tc_mma_f16(tmem + O_COL, pd, vd, IDO, (j | kk) != 0);   // O accumulates in TMEM
                 }
-                tc_commit(o_full);
+                tc_commit(pv_done(j & 1));
                 tc_commit(kv_empty(s));
             }
             if (!ok) {
@@ -187,11 +207,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         float *xs = xm + 2 * 2 * BQ;                                // [half][row]
         constexpr int HK = BKV / 2;                                 // keys per warp per block
         constexpr int HD = DH / 2;                                  // output columns per warp
-        float o[HD];
-#pragma unroll
-        for (int c = 0; c < HD; ++c) o[c] = 0.f;
-        float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-        uint8_t *prow = smem + OFF_P + half * (P_BYTES / 2) + row * 128;
+        float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nkb; ++j) {
             if (!mbar_wait(s_full, j & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
@@ -223,29 +239,36 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             xm[((j & 1) * 2 + half) * BQ + row] = mr;
             mbar_arrive(xmax_bar(q4));
             if (!mbar_wait(xmax_bar(q4), j & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
-            mr = fmaxf(mr, xm[((j & 1) * 2 + (half ^ 1)) * BQ + row]);
-            const float mx = fmaxf(m, mr * g.scale_log2);
-            const float alpha = ex2_approx(m - mx);   // m = -inf on the first block -> 0
+            mr = fmaxf(mr, xm[((j & 1) * 2 + (half ^ 1)) * BQ + row]) * g.scale_log2;
+            // lazy rescale: keep the reference max unless this block exceeds it by 2^8
+            const float m_new = mr > m + RESCALE_LOG2 ? mr : m;
+            const float alpha = m_new == m ? 1.f : ex2_approx(m - m_new);   // 0 on the first block
             float sum = 0.f;
 #pragma unroll
             for (int c = 0; c < HK; ++c) {
-                sv[c] = ex2_approx(fmaf(sv[c], g.scale_log2, -mx));
+                sv[c] = ex2_approx(fmaf(sv[c], g.scale_log2, -m_new));
                 sum += sv[c];
             }
             l = l * alpha + sum;                      // this warp's half of the row sum
-            m = mx;
-            // fold O_{j-1} (this warp's half of the columns); then P and O are free
-            if (j > 0) {
-                if (!mbar_wait(o_full, (j - 1) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
+            m = m_new;
+            // O (in TMEM) holds P_0..P_{j-1} V: rescale this warp's 32 columns in
+            // place when a row's reference max moved (both warps of the pair see
+            // the same rows, so they decide alike)
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                if (!mbar_wait(pv_done((j - 1) & 1), ((j - 1) >> 1) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
                 tc_fence_after();
                 uint32_t r[32];
                 tmem_ld32(tl + O_COL + half * HD, r);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < HD; ++i) o[i] = o[i] * alpha_prev + __uint_as_float(r[i]);
+                for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                tmem_st32(tl + O_COL + half * HD, r);
+                tmem_st_wait();
             }
-            alpha_prev = alpha;
+            // P buffer j & 1 was last read by P_{j-2} V_{j-2}
+            if (j >= 2 && !mbar_wait(pv_done(j & 1), ((j >> 1) - 1) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
             // P_j as fp16: this warp's 64 keys are panel `half` of the swizzled A tile
+            uint8_t *prow = smem + OFF_P + (j & 1) * P_BYTES + half * (P_BYTES / 2) + row * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 uint32_t hv[4];
@@ -261,13 +284,12 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full);
         }
-        if (ok && nkb > 0 && mbar_wait(o_full, (nkb - 1) & 1, g.err, ERR_WAIT_EPILOGUE)) {
+        if (ok && nkb > 0 &&
+            mbar_wait(pv_done((nkb - 1) & 1), ((nkb - 1) >> 1) & 1, g.err, ERR_WAIT_EPILOGUE)) {
             tc_fence_after();
             uint32_t r[32];
             tmem_ld32(tl + O_COL + half * HD, r);
             tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < HD; ++i) o[i] = o[i] * alpha_prev + __uint_as_float(r[i]);
             // the row sum is the two halves' sum (a + b == b + a: both warps agree)
             xs[half * BQ + row] = l;
             mbar_arrive(xsum_bar(q4));
@@ -283,7 +305,8 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                         uint32_t w[4];
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
-                            __half2 p = __floats2half2_rn(o[c + 2 * i] * inv, o[c + 2 * i + 1] * inv);
+                            __half2 p = __floats2half2_rn(__uint_as_float(r[c + 2 * i]) * inv,
+                                                          __uint_as_float(r[c + 2 * i + 1]) * inv);
                             w[i] = *reinterpret_cast<uint32_t *>(&p);
                         }
                         *reinterpret_cast<uint4 *>(dst + c) = make_uint4(w[0], w[1], w[2], w[3]);
