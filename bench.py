@@ -19,7 +19,7 @@ the full output on one rank) is timed separately and reported, not included.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Prints one JSON line (rank 0).  See DESIGN.md for the roofline arithmetic.
+Prints one JSON line (rank 0).
 """
 from __future__ import annotations
 

@@ -39,6 +39,13 @@ int rocket_activation_fp16(int fd, int kind, const _Float16 *in, _Float16 *out, 
 int rocket_ew_mul_fp16(int fd, const _Float16 *a, const _Float16 *b, _Float16 *out, int n);
 int rocket_ew_add_fp16(int fd, const _Float16 *a, const _Float16 *b, _Float16 *out, int n);
 int rocket_ew_sub_fp16(int fd, const _Float16 *a, const _Float16 *b, _Float16 *out, int n);
+/* out[i] = max / min(a[i], b[i]) (reference include/rocket_activation.h:170-173) */
+int rocket_ew_max_fp16(int fd, const _Float16 *a, const _Float16 *b, _Float16 *out, int n);
+int rocket_ew_min_fp16(int fd, const _Float16 *a, const _Float16 *b, _Float16 *out, int n);
+/* out[i] = min(max(in[i], lo), hi) (reference include/rocket_activation.h:178) */
+int rocket_clip_fp16(int fd, float lo, float hi, const _Float16 *in, _Float16 *out, int n);
+/* "gelu", "silu", ... ; "?" for an unknown kind (reference include/rocket_activation.h:237) */
+const char *rocket_activation_name(int kind);
 #ifdef __cplusplus
 }
 #endif

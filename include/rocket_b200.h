@@ -57,16 +57,31 @@ int   rocket_b200_profile_get(int idx, const char **name, uint64_t *launches, do
  *     device (A and Cf 16-byte aligned); nothing is copied.
  *   - A call needing more than the 32 MiB array (about N*K/2 + 2*M*K bytes)
  *     returns ROCKET_E_NOMEM and does nothing.
- *   - `stream` is a cudaStream_t (NULL = legacy default stream); the call
- *     waits for it before returning its status.
- *   - The first call on a device looks up the array's device address; make
- *     that first call before any stream capture.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  The call
+ *     is synchronous: it waits for the stream and reads the kernel's status
+ *     word before it returns.
+ *   - The first call on a device looks up the array's device address (a
+ *     one-time set-up on that device); make that first call before any
+ *     stream capture.
  *   - Every call on a device shares the one array, so calls that may overlap
  *     on the GPU (other streams, other host threads) race: serialise them. */
 int rocket_b200_matmul_int4_groupwise_noalloc(int M, int K, int N, const int8_t *A,
                                               const int8_t *B, const float *a_scale,
                                               const float *b_scale, float *Cf, int group,
                                               void *stream);
+
+/* Group-wise matmul mode for this process (rocket_matmul_int8_groupwise,
+ * rocket_matmul_int4_groupwise and the resident _gw entries).
+ *   0  precise (default): the reference's definition -- exact integer partial
+ *      per K group, scaled by a_scale[m,g] * b_scale[n,g] and summed across
+ *      groups in fp32 (src/rocket_matmul.c:2842-2856 of the reference); about
+ *      1e-7 relative to the fp64 value, inside its gates' 1e-5 * rms bound.
+ *   1  fast: w * b_scale (and a * a_scale when it varies with g) rounded to
+ *      fp16 once before an fp16 MMA; about 3e-4 relative Frobenius error.
+ * The environment variable ROCKET_GW_FAST=1 selects mode 1 until this is
+ * called.  No counterpart in the reference, which has only the first.
+ * Returns 0, or ROCKET_E_SHAPE for another value. */
+int rocket_b200_gw_mode(int mode);
 
 /* Batched encoder block: nb independent sequences of T tokens stacked along
  * rows (x and out are [nb*T, d]); every projection runs once over all nb*T

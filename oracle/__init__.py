@@ -122,6 +122,15 @@ def gw_f32(A, B, a_scale, b_scale, group):
 
 
 # ---- tolerance metrics used by the parity tests ----
+def rms_normalised_err(got, ref):
+    """max |got - ref| / rms(ref): the reference's group-wise gates bound this
+    by 1e-5 (tests/matmul_int8_groupwise_rocket.c:59-82)."""
+    ref = np.asarray(ref, np.float64)
+    rms = float(np.sqrt(np.mean(ref * ref)))
+    d = np.abs(np.asarray(got, np.float64) - ref)
+    return float(d.max()) / rms if rms > 0 else float(d.max())
+
+
 def rel_frobenius(got, ref):
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)

@@ -123,6 +123,13 @@ _SIGS += [
     ("rocket_ew_mul_fp16", c_int, [c_int, _P, _P, _P, c_int]),
     ("rocket_ew_add_fp16", c_int, [c_int, _P, _P, _P, c_int]),
     ("rocket_ew_sub_fp16", c_int, [c_int, _P, _P, _P, c_int]),
+    ("rocket_ew_max_fp16", c_int, [c_int, _P, _P, _P, c_int]),
+    ("rocket_ew_min_fp16", c_int, [c_int, _P, _P, _P, c_int]),
+    ("rocket_clip_fp16", c_int, [c_int, c_float, c_float, _P, _P, c_int]),
+    ("rocket_activation_name", c_char_p, [c_int]),
+    # rocket_hw_profile.h
+    ("rocket_hw_current", c_void_p, []),
+    ("rocket_hw_by_name", c_void_p, [c_char_p]),
     ("rocket_geglu_fp16", c_int, [c_int, _P, _P, c_int, _P, c_int]),
     ("rocket_ffn_fp16", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, _P]),
     ("rocket_ffn_fp16_fused", c_int, [c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, _P]),
@@ -158,6 +165,7 @@ _SIGS += [
     ("rocket_matmul_fp16_stream", c_int, [_P, c_int, c_int, c_int, _P, _P, _P]),
     ("rocket_matmul_fp16_stream_fused", c_int, [_P, c_int, c_int, _P, _P, c_int, _P, _P]),
     ("rocket_b200_gemm_policy", c_int, [c_int, c_int]),
+    ("rocket_b200_gw_mode", c_int, [c_int]),
     ("rocket_fa_ctx_create", _P, [c_int]),
     ("rocket_fa_ctx_free", None, [_P]),
     ("rocket_flash_attn_fp16", c_int, [c_int] * 7 + [c_float, c_float] + [_P] * 5),

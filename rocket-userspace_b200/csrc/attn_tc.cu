@@ -210,7 +210,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nkb; ++j) {
-            if (!mbar_wait(s_full, j & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
+            if (!mbar_wait_warp(s_full, j & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
             tc_fence_after();
             float sv[HK];
 #pragma unroll
@@ -238,7 +238,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             // exchange half-block maxima with the partner warp (bounded wait)
             xm[((j & 1) * 2 + half) * BQ + row] = mr;
             mbar_arrive(xmax_bar(q4));
-            if (!mbar_wait(xmax_bar(q4), j & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
+            if (!mbar_wait_warp(xmax_bar(q4), j & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
             mr = fmaxf(mr, xm[((j & 1) * 2 + (half ^ 1)) * BQ + row]) * g.scale_log2;
             // lazy rescale: keep the reference max unless this block exceeds it by 2^8
             const float m_new = mr > m + RESCALE_LOG2 ? mr : m;
@@ -255,7 +255,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             // place when a row's reference max moved (both warps of the pair see
             // the same rows, so they decide alike)
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-                if (!mbar_wait(pv_done((j - 1) & 1), ((j - 1) >> 1) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
+                if (!mbar_wait_warp(pv_done((j - 1) & 1), ((j - 1) >> 1) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
                 tc_fence_after();
                 uint32_t r[32];
                 tmem_ld32(tl + O_COL + half * HD, r);
@@ -266,7 +266,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                 tmem_st_wait();
             }
             // P buffer j & 1 was last read by P_{j-2} V_{j-2}
-            if (j >= 2 && !mbar_wait(pv_done(j & 1), ((j >> 1) - 1) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
+            if (j >= 2 && !mbar_wait_warp(pv_done(j & 1), ((j >> 1) - 1) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
             // P_j as fp16: this warp's 64 keys are panel `half` of the swizzled A tile
             uint8_t *prow = smem + OFF_P + (j & 1) * P_BYTES + half * (P_BYTES / 2) + row * 128;
 #pragma unroll
@@ -285,7 +285,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             if (lane == 0) mbar_arrive(p_full);
         }
         if (ok && nkb > 0 &&
-            mbar_wait(pv_done((nkb - 1) & 1), ((nkb - 1) >> 1) & 1, g.err, ERR_WAIT_EPILOGUE)) {
+            mbar_wait_warp(pv_done((nkb - 1) & 1), ((nkb - 1) >> 1) & 1, g.err, ERR_WAIT_EPILOGUE)) {
             tc_fence_after();
             uint32_t r[32];
             tmem_ld32(tl + O_COL + half * HD, r);
@@ -293,7 +293,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             // the row sum is the two halves' sum (a + b == b + a: both warps agree)
             xs[half * BQ + row] = l;
             mbar_arrive(xsum_bar(q4));
-            if (mbar_wait(xsum_bar(q4), 0, g.err, ERR_WAIT_EPILOGUE)) {
+            if (mbar_wait_warp(xsum_bar(q4), 0, g.err, ERR_WAIT_EPILOGUE)) {
                 const float lt = l + xs[(half ^ 1) * BQ + row];
                 const int t = qt * BQ + row;
                 if (t < g.T) {

@@ -43,8 +43,10 @@ RKB_DEV uint64_t global_timer_ns() {
 }
 
 // Hardware base-2 exponential (MUFU, flush-to-zero).  Used for softmax
-// weights, whose arguments are <= 0 (score minus running max): the result is
-// in [0, 1], -inf gives 0, and the ~2 ulp error is far below fp16 resolution.
+// weights.  With lazy rescaling (the running max is only moved when a row max
+// grows by more than 2^8 in log2 units) the arguments are <= 8, so weights are
+// < 2^8 (safe in fp16) and -inf gives 0; row sums and O stay in fp32.  The
+// ~2 ulp error is far below fp16 resolution.
 RKB_DEV float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -8,23 +8,33 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include "../src/rkb_kernels.h"
+#include "rkb_wlayout.cuh"
 #include "../../include/rocket_npu.h"
 
 namespace {
 
-constexpr int TILE_N = 256;
+// dst byte i -> (tile t, block kb, row r, byte j) of the ragged tiled layout
+// (rkb_wlayout.cuh); rb = bytes per row of one 64-wide K block
+__device__ __forceinline__ void wl_decode(size_t i, int N, int nkb, int rb, int &n, int &kb, int &j) {
+    const size_t tile_bytes = static_cast<size_t>(nkb) * rkb::WL_TILE * rb;
+    int t = static_cast<int>(i / tile_bytes);
+    const int last = rkb::wl_ntiles(N) - 1;
+    t = t > last ? last : t;
+    const size_t local = i - static_cast<size_t>(t) * tile_bytes;
+    const size_t blk = static_cast<size_t>(rkb::wl_rows(N, t)) * rb;
+    kb = static_cast<int>(local / blk);
+    const int rem = static_cast<int>(local % blk);
+    n = t * rkb::WL_TILE + rem / rb;
+    j = rem % rb;
+}
 
 __global__ void pack_codes_i8(const int8_t *__restrict__ src, int N, int K, int nkb,
                               uint8_t *__restrict__ dst, size_t total) {
-    // dst index -> (nt, kb, r, j): block of 256 x 64 bytes
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const int j = static_cast<int>(i & 63);
-        const int r = static_cast<int>((i >> 6) & 255);
-        const size_t blk = i >> 14;
-        const int kb = static_cast<int>(blk % nkb);
-        const int nt = static_cast<int>(blk / nkb);
-        const int n = nt * TILE_N + r, k = kb * 64 + j;
+        int n, kb, j;
+        wl_decode(i, N, nkb, 64, n, kb, j);
+        const int k = kb * 64 + j;
         int8_t v = (n < N && k < K) ? src[static_cast<size_t>(n) * K + k] : 0;
         dst[i] = static_cast<uint8_t>(v) ^ 0x80u;
     }
@@ -32,15 +42,12 @@ __global__ void pack_codes_i8(const int8_t *__restrict__ src, int N, int K, int 
 
 __global__ void pack_codes_i4(const int8_t *__restrict__ src, int N, int K, int nkb,
                               uint8_t *__restrict__ dst, size_t total) {
-    // block of 256 rows x 32 bytes; byte j holds codes 2j (low) and 2j+1 (high)
+    // rows of 32 bytes; byte j holds codes 2j (low nibble) and 2j+1 (high)
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const int j = static_cast<int>(i & 31);
-        const int r = static_cast<int>((i >> 5) & 255);
-        const size_t blk = i >> 13;
-        const int kb = static_cast<int>(blk % nkb);
-        const int nt = static_cast<int>(blk / nkb);
-        const int n = nt * TILE_N + r, k = kb * 64 + 2 * j;
+        int n, kb, j;
+        wl_decode(i, N, nkb, 32, n, kb, j);
+        const int k = kb * 64 + 2 * j;
         int v0 = 0, v1 = 0;
         if (n < N) {
             const int8_t *row = src + static_cast<size_t>(n) * K;
@@ -51,14 +58,17 @@ __global__ void pack_codes_i4(const int8_t *__restrict__ src, int N, int K, int 
     }
 }
 
-// Tiled fp16 scales [ntile][kblock64][256 rows][2 halves]: one thread per
-// weight row of a 256-row tile, 16 K-blocks per block; both halves of a
-// K-block go out as one coalesced 32-bit word.  bs == nullptr writes 1.0.
+// Tiled fp16 scales, rows of 2 halves (one per 32-wide K half of a block) in
+// the same ragged layout: one thread per weight row of a tile, 16 K-blocks
+// per CUDA block; each row's pair goes out as one 32-bit word.  bs == nullptr
+// writes 1.0.
 __global__ void pack_scales(const float *__restrict__ bs, int N, int K, int group, int nkb,
                             uint32_t *__restrict__ dst) {
-    const int r = threadIdx.x;                 // blockDim.x == TILE_N
+    const int r = threadIdx.x;                 // blockDim.x == WL_TILE
     const int nt = blockIdx.y;
-    const int n = nt * TILE_N + r;
+    const int rows = rkb::wl_rows(N, nt);
+    if (r >= rows) return;
+    const int n = nt * rkb::WL_TILE + r;
     const int nG = K / group;
     const int kb0 = blockIdx.x * 16;
     const int kb1 = kb0 + 16 < nkb ? kb0 + 16 : nkb;
@@ -70,7 +80,7 @@ __global__ void pack_scales(const float *__restrict__ bs, int N, int K, int grou
             s1 = (n < N && k1 < K) ? bs[static_cast<size_t>(n) * nG + k1 / group] : 0.0f;
         }
         __half2 h = __floats2half2_rn(s0, s1);
-        dst[(static_cast<size_t>(nt) * nkb + kb) * TILE_N + r] = *reinterpret_cast<uint32_t *>(&h);
+        dst[rkb::wl_block(N, nkb, nt, kb, 4) / 4 + r] = *reinterpret_cast<uint32_t *>(&h);
     }
 }
 
@@ -120,6 +130,18 @@ __global__ void gather_row_scale(const float *__restrict__ as, int M, int nG, fl
     if (m < M) dst[m] = as[static_cast<size_t>(m) * nG];
 }
 
+// a_scale [M, nG] -> [nG, M]: the precise group-wise epilogue reads one
+// group's activation scales for 32 consecutive tokens with one load per lane
+__global__ void scale_transpose(const float *__restrict__ as, int M, int nG, float *__restrict__ dst) {
+    const size_t total = static_cast<size_t>(M) * nG;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int m = static_cast<int>(i % M);
+        const int g = static_cast<int>(i / M);
+        dst[i] = as[static_cast<size_t>(m) * nG + g];
+    }
+}
+
 int grid_for(size_t total, int threads) {
     size_t b = (total + threads - 1) / threads;
     if (b > 148 * 16) b = 148 * 16;
@@ -133,15 +155,11 @@ int status(cudaError_t e) { return e == cudaSuccess ? 0 : ROCKET_E_DEVICE; }
 extern "C" {
 
 size_t rkb_wpack_codes_bytes(int N, int K, int bits) {
-    const size_t nt = (N + TILE_N - 1) / TILE_N;
-    const size_t nkb = (K + 127) / 128 * 2;
-    return nt * nkb * TILE_N * 64 * bits / 8;
+    return rkb::wl_bytes(N, K, 64 * bits / 8);
 }
 
 size_t rkb_wpack_scales_bytes(int N, int K) {
-    const size_t nt = (N + TILE_N - 1) / TILE_N;
-    const size_t nkb = (K + 127) / 128 * 2;
-    return nt * nkb * TILE_N * 2 * sizeof(__half);
+    return rkb::wl_bytes(N, K, 2 * sizeof(__half));
 }
 
 int rkb_wpack_codes(const int8_t *src, int N, int K, int bits, void *dst, cudaStream_t s) {
@@ -158,9 +176,9 @@ int rkb_wpack_codes(const int8_t *src, int N, int K, int bits, void *dst, cudaSt
 
 int rkb_wpack_scales(const float *b_scale, int N, int K, int group, void *dst, cudaStream_t s) {
     const int nkb = (K + 127) / 128 * 2;
-    const int ntiles = (N + TILE_N - 1) / TILE_N;
+    const int ntiles = rkb::wl_ntiles(N);
     if (ntiles > 65535) return ROCKET_E_SHAPE;
-    pack_scales<<<dim3((nkb + 15) / 16, ntiles), TILE_N, 0, s>>>(b_scale, N, K, group, nkb,
+    pack_scales<<<dim3((nkb + 15) / 16, ntiles), rkb::WL_TILE, 0, s>>>(b_scale, N, K, group, nkb,
                                                                  static_cast<uint32_t *>(dst));
     return status(cudaGetLastError());
 }
@@ -180,6 +198,12 @@ int rkb_prescale_a(const int8_t *A, const float *a_scale, int M, int K, int grou
         prescale_a<false><<<dim3(gx, gy), 256, 0, s>>>(A, a_scale, M, K, group, static_cast<__half *>(dst));
     else
         return ROCKET_E_SHAPE;
+    return status(cudaGetLastError());
+}
+
+int rkb_scale_transpose(const float *a_scale, int M, int nG, float *dst, cudaStream_t s) {
+    const size_t total = static_cast<size_t>(M) * nG;
+    scale_transpose<<<grid_for(total, 256), 256, 0, s>>>(a_scale, M, nG, dst);
     return status(cudaGetLastError());
 }
 

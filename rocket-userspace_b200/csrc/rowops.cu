@@ -219,44 +219,42 @@ __device__ __forceinline__ float act_eval(int kind, float x) {
     }
 }
 
-// op: 0 act(a), 1 a+b, 2 a*b, 3 a-b, 4 act(a)*b
-__global__ void elementwise(const __half *__restrict__ a, const __half *__restrict__ b, int op,
-                            int kind, size_t n, __half *__restrict__ out) {
+// op: 0 act(a), 1 a+b, 2 a*b, 3 a-b, 4 act(a)*b, 5 max(a,b), 6 min(a,b),
+// 7 clip(a, lo, hi).  The op is a template parameter so each kernel's inner
+// loop is branch-free; 16-byte loads and stores (8 halves) per thread.
+template <int OP>
+__device__ __forceinline__ float ew_eval(int kind, float x, float y, float lo, float hi) {
+    if (OP == 0) return act_eval(kind, x);
+    if (OP == 1) return x + y;
+    if (OP == 2) return x * y;
+    if (OP == 3) return x - y;
+    if (OP == 4) return act_eval(kind, x) * y;
+    if (OP == 5) return fmaxf(x, y);
+    if (OP == 6) return fminf(x, y);
+    return fminf(fmaxf(x, lo), hi);
+}
+
+template <int OP>
+__global__ void elementwise(const __half *__restrict__ a, const __half *__restrict__ b, int kind,
+                            float lo, float hi, size_t n, __half *__restrict__ out) {
+    constexpr bool TWO = OP >= 1 && OP <= 6;
     const size_t nv = n / 8;
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < nv; i += stride) {
         uint4 ua = reinterpret_cast<const uint4 *>(a)[i];
-        uint4 ub = b ? reinterpret_cast<const uint4 *>(b)[i] : make_uint4(0, 0, 0, 0);
+        uint4 ub = TWO ? reinterpret_cast<const uint4 *>(b)[i] : make_uint4(0, 0, 0, 0);
         const __half *ha = reinterpret_cast<const __half *>(&ua);
         const __half *hb = reinterpret_cast<const __half *>(&ub);
         uint4 w;
         __half *wh = reinterpret_cast<__half *>(&w);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float x = __half2float(ha[j]), y = __half2float(hb[j]);
-            float r;
-            switch (op) {
-            case 0: r = act_eval(kind, x); break;
-            case 1: r = x + y; break;
-            case 2: r = x * y; break;
-            case 3: r = x - y; break;
-            default: r = act_eval(kind, x) * y; break;
-            }
-            wh[j] = __float2half_rn(r);
-        }
+        for (int j = 0; j < 8; ++j)
+            wh[j] = __float2half_rn(ew_eval<OP>(kind, __half2float(ha[j]), __half2float(hb[j]), lo, hi));
         reinterpret_cast<uint4 *>(out)[i] = w;
     }
     for (size_t i = nv * 8 + blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += stride) {
-        const float x = __half2float(a[i]), y = b ? __half2float(b[i]) : 0.f;
-        float r;
-        switch (op) {
-        case 0: r = act_eval(kind, x); break;
-        case 1: r = x + y; break;
-        case 2: r = x * y; break;
-        case 3: r = x - y; break;
-        default: r = act_eval(kind, x) * y; break;
-        }
-        out[i] = __float2half_rn(r);
+        const float x = __half2float(a[i]), y = TWO ? __half2float(b[i]) : 0.f;
+        out[i] = __float2half_rn(ew_eval<OP>(kind, x, y, lo, hi));
     }
 }
 
@@ -407,13 +405,29 @@ int rkb_softmax_rows(const void *x, int M, int N, int log_mode, void *out, cudaS
 
 int rkb_elementwise(const void *a, const void *b, int op, int kind, size_t n, void *out,
                     cudaStream_t s) {
-    if (n == 0) return ROCKET_E_SHAPE;
+    return rkb_elementwise_ex(a, b, op, kind, 0.f, 0.f, n, out, s);
+}
+
+int rkb_elementwise_ex(const void *a, const void *b, int op, int kind, float lo, float hi, size_t n,
+                       void *out, cudaStream_t s) {
+    if (n == 0 || op < 0 || op > 7) return ROCKET_E_SHAPE;
+    if ((op >= 1 && op <= 6) && !b) return ROCKET_E_SHAPE;
     if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
          reinterpret_cast<uintptr_t>(out)) & 15)
         return ROCKET_E_SHAPE;
-    elementwise<<<grid_for(n / 8 + 1, 256), 256, 0, s>>>(static_cast<const __half *>(a),
-                                                         static_cast<const __half *>(b), op, kind, n,
-                                                         static_cast<__half *>(out));
+    const __half *ha = static_cast<const __half *>(a), *hb = static_cast<const __half *>(b);
+    __half *ho = static_cast<__half *>(out);
+    const int grid = grid_for(n / 8 + 1, 256);
+    switch (op) {
+    case 0: elementwise<0><<<grid, 256, 0, s>>>(ha, hb, kind, lo, hi, n, ho); break;
+    case 1: elementwise<1><<<grid, 256, 0, s>>>(ha, hb, kind, lo, hi, n, ho); break;
+    case 2: elementwise<2><<<grid, 256, 0, s>>>(ha, hb, kind, lo, hi, n, ho); break;
+    case 3: elementwise<3><<<grid, 256, 0, s>>>(ha, hb, kind, lo, hi, n, ho); break;
+    case 4: elementwise<4><<<grid, 256, 0, s>>>(ha, hb, kind, lo, hi, n, ho); break;
+    case 5: elementwise<5><<<grid, 256, 0, s>>>(ha, hb, kind, lo, hi, n, ho); break;
+    case 6: elementwise<6><<<grid, 256, 0, s>>>(ha, hb, kind, lo, hi, n, ho); break;
+    default: elementwise<7><<<grid, 256, 0, s>>>(ha, hb, kind, lo, hi, n, ho); break;
+    }
     return status();
 }
 

@@ -21,9 +21,9 @@
 //   warps 2..5   epilogue (TMEM -> registers -> global)
 //   warps 6..13  dequantisers: raw stage -> 128-byte-swizzled operand tile
 //
-// Resident weight layout (written by rkb_wpack_codes / rkb_wpack_scales): for
-// N tile nt (256 rows) and K block kb (64 codes) a contiguous block of
-// 256 x 64 codes, row-major inside the block; int8 codes are stored offset by
+// Resident weight layout (written by rkb_wpack_codes / rkb_wpack_scales, see
+// rkb_wlayout.cuh): for N tile nt (256 rows; the last tile only its own rows)
+// and K block kb (64 codes) a contiguous block of rows x 64 codes, row-major; int8 codes are stored offset by
 // +128 (u8 = v ^ 0x80) and int4 codes offset by +8 (two per byte, even k in the
 // low nibble), so the dequantiser can build fp16 values with byte permutes.
 #include <cuda.h>
@@ -37,6 +37,7 @@
 
 #include "rkb_ptx.cuh"
 #include "rkb_tmap.h"
+#include "rkb_wlayout.cuh"
 #include "../src/rkb_kernels.h"
 #include "../../include/rocket_npu.h"
 
@@ -246,19 +247,28 @@ wgemm_kernel(const __grid_constant__ CUtensorMap tmA, const Args g) {
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 const int mt = t % g.m_tiles, nt = t / g.m_tiles;
-                const uint8_t *tile_codes =
-                    g.codes + static_cast<size_t>(nt) * g.kb64_total * Cfg<MODE_F16, WBITS>::CODE_BLOCK;
-                const __half *tile_scales =
-                    g.scales + static_cast<size_t>(nt) * g.kb64_total * (BN * 2);
+                // ragged layout: the last N tile stores only its own rows (the
+                // rest of the stage keeps stale, finite data; those rows are
+                // never stored)
+                constexpr int RB = 64 * WBITS / 8;
+                const int rows = wl_rows(g.N, nt);
+                const uint32_t blk = static_cast<uint32_t>(rows * RB);
+                const uint32_t tx = C::A_BYTES + (MODE == MODE_F16 ? blk + rows * 4 : 2 * blk);
                 for (int kb = 0; kb < g.k_blocks; ++kb) {
                     if (!mbar_wait(raw_empty(r), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) { ok = false; break; }
-                    mbar_arrive_expect_tx(raw_full(r), C::TX_BYTES);
+                    mbar_arrive_expect_tx(raw_full(r), tx);
                     tma_load_2d(sA(r), &tmA, kb * A_BK_ELEMS, mt * BM, raw_full(r));
-                    bulk_load(sCode(r), tile_codes + static_cast<size_t>(kb) * C::CODE_BYTES,
-                              C::CODE_BYTES, raw_full(r));
-                    if (MODE == MODE_F16)
-                        bulk_load(sScale(r), tile_scales + static_cast<size_t>(kb) * (BN * 2),
-                                  C::SCALE_BYTES, raw_full(r));
+                    if (MODE == MODE_F16) {
+                        bulk_load(sCode(r), g.codes + wl_block(g.N, g.kb64_total, nt, kb, RB), blk, raw_full(r));
+                        bulk_load(sScale(r),
+                                  reinterpret_cast<const uint8_t *>(g.scales) + wl_block(g.N, g.kb64_total, nt, kb, 4),
+                                  rows * 4, raw_full(r));
+                    } else {
+                        // two 64-wide K blocks per 128-wide MMA K block, 256 rows apart in shared memory
+                        bulk_load(sCode(r), g.codes + wl_block(g.N, g.kb64_total, nt, 2 * kb, RB), blk, raw_full(r));
+                        bulk_load(sCode(r) + Cfg<MODE_F16, WBITS>::CODE_BLOCK,
+                                  g.codes + wl_block(g.N, g.kb64_total, nt, 2 * kb + 1, RB), blk, raw_full(r));
+                    }
                     if (++r == RS) { r = 0; ph ^= 1; }
                 }
             }

@@ -43,6 +43,7 @@
 
 #include "rkb_ptx.cuh"
 #include "rkb_tmap.h"
+#include "rkb_wlayout.cuh"
 #include "../src/rkb_kernels.h"
 #include "../../include/rocket_npu.h"
 
@@ -138,11 +139,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 wgemm_ts_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
     using C = Cfg<WBITS>;
     constexpr int RS = C::RS;
-    constexpr int BLOCK = 256 * 64 * WBITS / 8;      // one resident 256-row x 64-K code block
     const int nh = g.nh, nt = 2 * nh;
     const int dstride = (nh + 31) & ~31;   // token half p at TMEM column p * dstride
     const uint32_t IDESC = idesc_f16_f32acc(WM, nh);
-    const int tx_bytes = nt * 128 + C::CODE_BYTES + C::SCALE_BYTES;
+    constexpr int RB = 64 * WBITS / 8;               // code bytes per row of a 64-wide K block
+    const int tx_b = nt * 128;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -202,17 +203,22 @@ wgemm_ts_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 const int mt = t % g.m_tiles, nt128 = t / g.m_tiles;   // nt128: 128-row weight tile
-                const uint8_t *codes = g.codes + static_cast<size_t>(nt128 >> 1) * g.kb64_total * BLOCK +
-                                       (nt128 & 1) * C::CODE_BYTES;
-                const __half *scales = g.scales + static_cast<size_t>(nt128 >> 1) * g.kb64_total * 512 +
-                                       (nt128 & 1) * 256;
+                // half h of 256-row tile t256 in the ragged layout (rkb_wlayout.cuh):
+                // rows past the weight's end are not stored and keep stale data
+                const int t256 = nt128 >> 1, h = nt128 & 1;
+                const int rows = wl_rows(g.N, t256);
+                const int hv = rows - h * WM < WM ? rows - h * WM : WM;
+                const uint32_t cbytes = static_cast<uint32_t>(hv * RB), sbytes = static_cast<uint32_t>(hv * 4);
                 for (int kb = 0; kb < g.k_blocks; ++kb) {
                     if (!mbar_wait(raw_empty(r), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) { ok = false; break; }
-                    mbar_arrive_expect_tx(raw_full(r), tx_bytes);
+                    mbar_arrive_expect_tx(raw_full(r), tx_b + cbytes + sbytes);
                     tma_load_2d(sBh(r, 0), &tmB, kb * 64, mt * nt, raw_full(r));
                     tma_load_2d(sBh(r, 1), &tmB, kb * 64, mt * nt + nh, raw_full(r));
-                    bulk_load(sCode(r), codes + static_cast<size_t>(kb) * BLOCK, C::CODE_BYTES, raw_full(r));
-                    bulk_load(sScale(r), scales + static_cast<size_t>(kb) * 512, C::SCALE_BYTES, raw_full(r));
+                    bulk_load(sCode(r), g.codes + wl_block(g.N, g.kb64_total, t256, kb, RB) + h * WM * RB,
+                              cbytes, raw_full(r));
+                    bulk_load(sScale(r),
+                              reinterpret_cast<const uint8_t *>(g.scales) + wl_block(g.N, g.kb64_total, t256, kb, 4) + h * WM * 4,
+                              sbytes, raw_full(r));
                     if (++r == RS) { r = 0; ph ^= 1; }
                 }
             }

@@ -68,12 +68,27 @@ typedef struct {
     const void *Ws;           /* tiled fp16 scales */
     void *C; long ldc; int out_kind;
     const float *row_scale;
+    /* exact-partial (precise) group-wise form only, rkb_wgemm_xp_run:
+     * A holds the unscaled int8 values as fp16, Ws is unused */
+    const float *b_scale;     /* fp32 [N, K/group] */
+    const float *a_scale_t;   /* fp32 [K/group, M] when a_scale varies with g, else NULL */
+    int group;
+    int seg;                  /* K per exact partial: rkb_wgemm_xp_segment(group, w_bits) */
 } rkb_wgemm_desc;
 
 int rkb_wgemm_run(const rkb_wgemm_desc *d, int *err_word, cudaStream_t stream);
 /* The a_f16 (group-wise) form with the dequantised weights fed from TMEM;
  * rkb_wgemm_run routes a_f16 descriptors here. */
 int rkb_wgemm_ts_run(const rkb_wgemm_desc *d, int *err_word, cudaStream_t stream);
+
+/* Precise group-wise form: per-segment exact integer partials (fp16 MMA on
+ * unscaled integer operands), scaled by b_scale[n,g] (x a_scale[m,g]) and
+ * summed across groups in fp32 in the epilogue.  row_scale, when given, is
+ * applied at the end (a_scale constant along g). */
+int rkb_wgemm_xp_run(const rkb_wgemm_desc *d, int *err_word, cudaStream_t stream);
+int rkb_wgemm_xp_segment(int group, int w_bits);
+/* a_scale [M, nG] -> [nG, M] */
+int rkb_scale_transpose(const float *a_scale, int M, int nG, float *dst, cudaStream_t s);
 
 /* Resident-weight packers (device -> device).  src is the row-major int8
  * weight [N, K] (values in [-8,7] when bits == 4); dst gets the tiled layout
@@ -97,9 +112,12 @@ int rkb_gather_row_scale(const float *a_scale, int M, int nG, float *dst, cudaSt
 int rkb_norm_rows(const void *x, const void *gamma, const void *beta, int M, int H, float eps,
                   int rms, void *out, cudaStream_t s);
 int rkb_softmax_rows(const void *x, int M, int N, int log_mode, void *out, cudaStream_t s);
-/* op: 0 act(a), 1 a+b, 2 a*b, 3 a-b, 4 act(a)*b; kind = rocket_activation_kind */
+/* op: 0 act(a), 1 a+b, 2 a*b, 3 a-b, 4 act(a)*b, 5 max(a,b), 6 min(a,b),
+ * 7 clip(a, lo, hi); kind = rocket_activation_kind */
 int rkb_elementwise(const void *a, const void *b, int op, int kind, size_t n, void *out,
                     cudaStream_t s);
+int rkb_elementwise_ex(const void *a, const void *b, int op, int kind, float lo, float hi, size_t n,
+                       void *out, cudaStream_t s);
 /* qkv [B*T, 3*H*dh] (row pitch ld) -> Q, K [B*H, Tp, dh], Vt [B*H, dh, Tp], zero padded */
 int rkb_split_heads(const void *qkv, long ld, int B, int T, int Tp, int H, int dh, void *Q,
                     void *K, void *Vt, cudaStream_t s);

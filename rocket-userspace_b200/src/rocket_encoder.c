@@ -98,24 +98,31 @@ int rocket_logsoftmax_fp16(int fd, int M, int N, const _Float16 *in, _Float16 *o
 }
 
 /* ---- element-wise ---------------------------------------------------------------- */
-static int ew_common(const char *who, int fd, const void *a, const void *b, int op, int kind,
-                     void *out, int n)
+static int ew_common2(const char *who, int fd, const void *a, const void *b, int op, int kind,
+                      float lo, float hi, void *out, int n)
 {
-    if (n <= 0 || !a || !out || (op && !b)) return ROCKET_E_SHAPE;
+    const int two = op >= 1 && op <= 6;
+    if (n <= 0 || !a || !out || (two && !b)) return ROCKET_E_SHAPE;
     rkb_call c;
     int rc = rkb_call_begin(&c, fd, who);
     if (rc) return rc;
     const size_t bytes = (size_t)n * 2;
     const void *da = rkb_call_in(&c, a, bytes);
-    const void *db = op ? rkb_call_in(&c, b, bytes) : NULL;
+    const void *db = two ? rkb_call_in(&c, b, bytes) : NULL;
     void *dout = rkb_call_out(&c, out, bytes);
     if (!c.rc) {
         int ps = rkb_prof_begin(c.h);
-        rkb_call_check(&c, rkb_elementwise(da, db, op, kind, (size_t)n, dout, c.h->stream));
+        rkb_call_check(&c, rkb_elementwise_ex(da, db, op, kind, lo, hi, (size_t)n, dout, c.h->stream));
         rkb_prof_end(c.h, ps, RKB_K_ELEMWISE);
         rkb_count(0, 1);
     }
     return rkb_call_end(&c);
+}
+
+static int ew_common(const char *who, int fd, const void *a, const void *b, int op, int kind,
+                     void *out, int n)
+{
+    return ew_common2(who, fd, a, b, op, kind, 0.f, 0.f, out, n);
 }
 
 static int kind_ok(int kind)
@@ -146,6 +153,34 @@ int rocket_ew_mul_fp16(int fd, const _Float16 *a, const _Float16 *b, _Float16 *o
 int rocket_ew_sub_fp16(int fd, const _Float16 *a, const _Float16 *b, _Float16 *out, int n)
 {
     return ew_common("rocket_ew_sub_fp16", fd, a, b, 3, 0, out, n);
+}
+
+/* max / min / clip (reference include/rocket_activation.h:170-178): one
+ * element-wise kernel each; clip is a single pass min(max(x, lo), hi). */
+int rocket_ew_max_fp16(int fd, const _Float16 *a, const _Float16 *b, _Float16 *out, int n)
+{
+    return ew_common("rocket_ew_max_fp16", fd, a, b, 5, 0, out, n);
+}
+
+int rocket_ew_min_fp16(int fd, const _Float16 *a, const _Float16 *b, _Float16 *out, int n)
+{
+    return ew_common("rocket_ew_min_fp16", fd, a, b, 6, 0, out, n);
+}
+
+int rocket_clip_fp16(int fd, float lo, float hi, const _Float16 *in, _Float16 *out, int n)
+{
+    if (!(lo <= hi)) return ROCKET_E_SHAPE;
+    return ew_common2("rocket_clip_fp16", fd, in, NULL, 7, 0, lo, hi, out, n);
+}
+
+/* Names as the reference prints them (src/rocket_activation.c:116-140). */
+const char *rocket_activation_name(int kind)
+{
+    static const char *const names[] = {
+        "sigmoid", "hardsigmoid", "hardswish", "silu", "tanh", "gelu", "leaky_relu", "sqrt",
+        "rsqrt", "reciprocal", "exp", "gelu_gate", "softplus", "mish_gate", "mish", "abs",
+        "elu", "selu", "log"};
+    return kind >= 0 && kind < (int)(sizeof names / sizeof names[0]) ? names[kind] : "?";
 }
 
 int rocket_geglu_fp16(int fd, const _Float16 *gate, const _Float16 *up, int kind, _Float16 *prod, int n)

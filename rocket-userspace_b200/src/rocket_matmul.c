@@ -13,6 +13,8 @@
 #include <string.h>
 
 #include "rocket_matmul.h"
+#include "rocket_b200.h"
+#include "rocket_hw_profile.h"
 #include "rkb_internal.h"
 
 /* ---- shape rules (reference API.md:96-104) ------------------------------ */
@@ -45,8 +47,21 @@ int rocket_matmul_plan_int8_gw(int M, int K, int N, int group, int *Mt, int *Kt,
 {
     if (!m_ok(M, 0) || K <= 0 || N <= 0 || K % 32 || N % 32 || !gw_group_ok(K, group))
         return ROCKET_E_SHAPE;
-    /* the kernel's K block (64) always lies inside one 32-aligned group slice */
-    return plan_common(M, K, N, 64, Mt, Kt, Nt);
+    /* Kt = K per exact integer partial: the group, or a piece of at most 1024
+     * of a wider one (the precise group-wise kernel's segment) */
+    return plan_common(M, K, N, rkb_wgemm_xp_segment(group, 8), Mt, Kt, Nt);
+}
+
+/* ---- hardware profile (reference include/rocket_hw_profile.h:60-108) ----- */
+static const struct rocket_hw_profile g_hw_b200 = {
+    "b200", 0, 0, 256, 16, 8, 16, ~0u, NULL, 1,
+};
+
+const struct rocket_hw_profile *rocket_hw_current(void) { return &g_hw_b200; }
+
+const struct rocket_hw_profile *rocket_hw_by_name(const char *name)
+{
+    return name && strcmp(name, "b200") == 0 ? &g_hw_b200 : NULL;
 }
 
 int rocket_matmul_plan_int4(int M, int K, int N, int *Mt, int *Kt, int *Nt)
@@ -83,6 +98,60 @@ int rkb_rows_const(const float *a_scale, int M, int nG)
     return 1;
 }
 
+/* Group-wise mode for this process: 0 precise (default), 1 fast.  The
+ * environment variable ROCKET_GW_FAST=1 selects the fast mode too. */
+static int g_gw_mode = -1;
+
+int rocket_b200_gw_mode(int mode)
+{
+    if (mode < 0 || mode > 1) return ROCKET_E_SHAPE;
+    __atomic_store_n(&g_gw_mode, mode, __ATOMIC_RELAXED);
+    return 0;
+}
+
+static int gw_fast(void)
+{
+    int m = __atomic_load_n(&g_gw_mode, __ATOMIC_RELAXED);
+    if (m < 0) m = rkb_env_long("ROCKET_GW_FAST", 0) ? 1 : 0;
+    return m == 1;
+}
+
+/* Precise form (the reference's definition, src/rocket_matmul.c:2842-2856):
+ * exact integer partials per group from the fp16 MMA on unscaled operands,
+ * scaled and summed across groups in fp32 by the kernel's epilogue. */
+static int gw_precise_on(rkb_handle *h, int M, int N, int K, int group, int w_bits,
+                         const int8_t *dA, const float *das, int a_rows_const,
+                         const void *dWq, const float *dbs, void *dC, long ldc, int out_kind)
+{
+    const int nG = K / group;
+    void *af = rkb_scratch(h, RKB_SCR_AUX, (size_t)M * K * 2);
+    float *sc = rkb_scratch(h, RKB_SCR_ROW, (size_t)M * (a_rows_const ? 1 : nG) * sizeof(float));
+    if (!af || !sc) return ROCKET_E_NOMEM;
+    int ps = rkb_prof_begin(h);
+    int rc = rkb_prescale_a(dA, NULL, M, K, group, af, h->stream);
+    if (!rc) rc = a_rows_const ? rkb_gather_row_scale(das, M, nG, sc, h->stream)
+                               : rkb_scale_transpose(das, M, nG, sc, h->stream);
+    rkb_prof_end(h, ps, RKB_K_PRESCALE);
+    if (rc) return rc;
+    rkb_wgemm_desc d;
+    memset(&d, 0, sizeof d);
+    d.M = M; d.N = N; d.K = K;
+    d.w_bits = w_bits; d.a_f16 = 1;
+    d.A = af; d.lda = K;
+    d.Wq = dWq;
+    d.C = dC; d.ldc = ldc; d.out_kind = out_kind;
+    d.row_scale = a_rows_const ? sc : NULL;
+    d.a_scale_t = a_rows_const ? NULL : sc;
+    d.b_scale = dbs;
+    d.group = group;
+    d.seg = rkb_wgemm_xp_segment(group, w_bits);
+    rkb_count(0, 3);
+    ps = rkb_prof_begin(h);
+    rc = rkb_wgemm_xp_run(&d, h->err_dev, h->stream);
+    rkb_prof_end(h, ps, w_bits == 4 ? RKB_K_WGEMM_W4_F16 : RKB_K_WGEMM_W8_F16);
+    return rc;
+}
+
 int rkb_gw_on(rkb_handle *h, int M, int N, int K, int group, int w_bits,
               const int8_t *dA, const float *a_scale, int a_rows_const,
               const void *dWq, const float *b_scale, void *dC, long ldc, int out_kind)
@@ -90,9 +159,15 @@ int rkb_gw_on(rkb_handle *h, int M, int N, int K, int group, int w_bits,
     const int nG = K / group;
     const float *dbs = rkb_stage_in(h, RKB_SCR_BS, b_scale, (size_t)N * nG * sizeof(float));
     const float *das = rkb_stage_in(h, RKB_SCR_AS, a_scale, (size_t)M * nG * sizeof(float));
+    if (!dbs || !das) return ROCKET_E_NOMEM;
+    if (!gw_fast())
+        return gw_precise_on(h, M, N, K, group, w_bits, dA, das, a_rows_const, dWq, dbs, dC, ldc,
+                             out_kind);
+    /* fast form: w * b_scale (and a * a_scale when it varies with g) rounded to
+     * fp16 once, fp32 accumulation (about 3e-4 relative) */
     void *ws = rkb_scratch(h, RKB_SCR_WS, rkb_wpack_scales_bytes(N, K));
     void *af = rkb_scratch(h, RKB_SCR_AUX, (size_t)M * K * 2);
-    if (!dbs || !das || !ws || !af) return ROCKET_E_NOMEM;
+    if (!ws || !af) return ROCKET_E_NOMEM;
     int ps = rkb_prof_begin(h);
     int rc = rkb_wpack_scales(dbs, N, K, group, ws, h->stream);
     rkb_prof_end(h, ps, RKB_K_PACK);

@@ -614,7 +614,7 @@ int rocket_matmul_fp16_stream_fused(rocket_stream *s, int M, int K, const _Float
         if (!Bs[i] || Ns[i] <= 0) return ROCKET_E_SHAPE;
         N += Ns[i];
     }
-    if (rocket_matmul_plan(M, K, N, NULL, NULL, NULL) < 0 || M % 4) return ROCKET_E_SHAPE;
+    if (rocket_matmul_plan(M, K, N, NULL, NULL, NULL) < 0) return ROCKET_E_SHAPE;
     int rc = rweights_fill(&s->r, &s->w, RW_F16, M, K, N, nseg, (const void *const *)Bs, Ns, 0, 0, who);
     if (rc) return rc;
     rrun_args a = { A, C, NULL, NULL, RKB_OUT_F16 };

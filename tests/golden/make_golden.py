@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory from the reference's own gates.
 
-Run in a container where the reference tree is mounted (default
-/root/reference).  For each gate below this script:
+Run where the reference checkout is present (ROCKET_REF, else a directory
+named "reference" beside this repository).  For each gate below this script:
   1. builds oracle/_ref/pin_<gate> (the reference's test program compiled
      unchanged, linked against oracle/ref_stub.c + oracle/oracle.c),
   2. runs it with ORC_DUMP set, so every matmul call the gate makes dumps its

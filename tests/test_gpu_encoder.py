@@ -226,3 +226,47 @@ def test_async_enqueue_with_device_operands(rkb, dev, orc, gi):
         rkb.lib.rocket_b200_set_async(0)
     check(orc, y.cpu().numpy(), GOLD["ln_y"])
     check(orc, ye.cpu().numpy(), GOLD["enc_y"])
+
+
+def test_mha_lazy_rescale(rkb, dev, orc):
+    """Scores that jump by far more than 2^8 (log2 units) in later key blocks,
+    so the head_dim-64 kernel's in-TMEM rescale of O (lazy rescaling) runs,
+    twice per row for the rows that see both jumps, with P double-buffered."""
+    T, d, nh = 384, 64, 1
+    p = orc.encoder_params(T, d, nh, 4 * d, 77)
+    x = orc.normal_f16(78, 0.3, (T, d)).astype(np.float32)
+    v = np.ones(T, np.float32)
+    v[[130, 131, 200]] = 3.0          # key block 1: raw score x5 per unit -> jump of ~10
+    v[[300, 301]] = 6.0               # key block 2: a second, larger jump
+    x[:, 0] = v
+    p["x"] = x.astype(np.float16)
+    Wq = orc.normal_f16(79, 0.02, (d, d)).astype(np.float32)
+    Wk = orc.normal_f16(80, 0.02, (d, d)).astype(np.float32)
+    Wq[0, :] = 0.0
+    Wk[0, :] = 0.0
+    Wq[0, 0] = 40.0                   # q_t[0] = 40 v_t, k_s[0] = v_s: scaled score 5 v_t v_s
+    Wk[0, 0] = 1.0
+    p["Wq"], p["Wk"] = Wq.astype(np.float16), Wk.astype(np.float16)
+    p["bq"] = np.zeros(d, np.float16)
+    p["bk"] = np.zeros(d, np.float16)
+    p["Wv"] = orc.normal_f16(81, 0.5, (d, d))
+    y = np.zeros((T, d), np.float16)
+    args = [P(rkb, p[k]) for k in ["x", "Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo"]]
+    assert rkb.lib.rocket_mha_self_fp16(dev.fd, T, d, nh, *args, P(rkb, y)) == 0
+    ref = orc.mha_self(p["x"], p["Wq"], p["bq"], p["Wk"], p["bk"], p["Wv"], p["bv"], p["Wo"], p["bo"], nh)
+    check(orc, y, ref)
+
+
+@pytest.mark.parametrize("n", [1, 8, 1003, 1 << 20])
+def test_ew_max_min_clip(rkb, dev, orc, n):
+    a = orc.normal_f16(n + 1, 2.0, (n,))
+    b = orc.normal_f16(n + 2, 2.0, (n,))
+    y = np.zeros(n, np.float16)
+    assert rkb.lib.rocket_ew_max_fp16(dev.fd, P(rkb, a), P(rkb, b), P(rkb, y), n) == 0
+    assert np.array_equal(y, np.maximum(a, b))
+    assert rkb.lib.rocket_ew_min_fp16(dev.fd, P(rkb, a), P(rkb, b), P(rkb, y), n) == 0
+    assert np.array_equal(y, np.minimum(a, b))
+    assert rkb.lib.rocket_clip_fp16(dev.fd, -1.0, 0.5, P(rkb, a), P(rkb, y), n) == 0
+    assert np.array_equal(y, np.clip(a, np.float16(-1.0), np.float16(0.5)))
+    assert rkb.lib.rocket_clip_fp16(dev.fd, 1.0, -1.0, P(rkb, a), P(rkb, y), n) == rkb.ROCKET_E_SHAPE
+    assert rkb.lib.rocket_activation_name(5) == b"gelu" and rkb.lib.rocket_activation_name(99) == b"?"

@@ -180,3 +180,33 @@ def test_async_enqueue_then_sync(rkb, dev, orc):
     for w in ws:
         rkb.lib.rocket_i8_weights_free(ctx, w)
     rkb.lib.rocket_i8_ctx_free(ctx)
+
+
+# The bench's headline path: resident per-channel int8 at M = 4096 on the
+# N-shard widths that one-rank-per-GPU runs use (QKV 5888, O 3840, gate+up
+# 30720 at K 3840; down 3840 at K 15360; split over 2 / 4 / 8 GPUs, rounded to
+# 32 as the reference's worker split does, or to the 256-wide tile).
+SHARDS = [(736, 3840), (480, 3840), (3840, 3840), (480, 15360), (2944, 3840), (1920, 3840),
+          (15360, 3840), (1920, 15360), (768, 3840), (512, 15360), (1472, 3840), (960, 15360)]
+
+
+@pytest.mark.parametrize("nsub,K", SHARDS, ids=[f"{n}x{k}" for n, k in SHARDS])
+def test_i8_resident_shard_widths_m4096(rkb, orc, nsub, K):
+    import torch
+    M = 4096
+    A = orc.uniform_i8(300 + nsub, -128, 127, (M, K))
+    B = orc.uniform_i8(400 + K, -128, 127, (nsub, K))
+    ctx = rkb.lib.rocket_i8_ctx_create(1)
+    assert ctx
+    w = rkb.lib.rocket_i8_weights_pack(ctx, M, K, nsub, rkb.ptr(B))
+    assert w
+    dA = torch.from_numpy(A).cuda()
+    dC = torch.full((M, nsub), -0x55555556, dtype=torch.int32, device="cuda")
+    rc = rkb.lib.rocket_matmul_int8_prepacked(ctx, M, K, nsub, rkb.ptr(dA), rkb.ptr(dC), w)
+    rkb.lib.rocket_i8_weights_free(ctx, w)
+    rkb.lib.rocket_i8_ctx_free(ctx)
+    assert rc == 0
+    C = dC.cpu().numpy()
+    # tile edges of the 128- and 256-row tilings, and the ends
+    rows = sorted({0, 1, 127, 128, 255, 256, 511, 512, 2047, 2048, 3839, 3840, 4094, 4095})
+    assert np.array_equal(C[rows], orc.matmul_int8(A[rows], B, nthreads=8))

@@ -10,7 +10,8 @@ import subprocess
 import pytest
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.environ.get("ROCKET_REF", "/root/reference")
+# the reference checkout: ROCKET_REF, else a directory named "reference" beside the repository
+REF = os.environ.get("ROCKET_REF") or os.path.join(os.path.dirname(REPO), "reference")
 ORACLE = os.path.join(REPO, "oracle")
 
 CASES = [
