@@ -73,9 +73,15 @@ static int rctx_init(rkb_rctx *c, int nthreads, int atom, const char *who)
             return ROCKET_E_DEVICE;
         }
     }
-    /* let slices copy straight into a peer GPU's output buffer */
-    for (int a = 0; a < nthreads && a < ndev; a++)
-        for (int b = 0; b < nthreads && b < ndev; b++) {
+    /* let slices copy straight into a peer GPU's output buffer: peer access
+     * between every pair of the devices the workers actually run on
+     * ((base + t) % ndev), leaving the caller's current device as it was */
+    int cur = 0;
+    cudaGetDevice(&cur);
+    const int nd = nthreads < ndev ? nthreads : ndev;
+    for (int i = 0; i < nd; i++)
+        for (int j = 0; j < nd; j++) {
+            const int a = (base + i) % ndev, b = (base + j) % ndev;
             if (a == b) continue;
             int can = 0;
             cudaDeviceCanAccessPeer(&can, a, b);
@@ -85,6 +91,7 @@ static int rctx_init(rkb_rctx *c, int nthreads, int atom, const char *who)
                 cudaGetLastError();   /* already enabled is fine */
             }
         }
+    cudaSetDevice(cur);
     return 0;
 }
 
@@ -238,6 +245,8 @@ static int rrun(const rkb_rctx *c, const rkb_rweights *w, int M, const rrun_args
     const size_t esz = w->kind == RW_F16 ? 2 : w->kind == RW_BF16 ? 4 : 1;
     const size_t osz = a->out_kind == RKB_OUT_F16 ? 2 : 4;
     const int c_dev = rkb_ptr_device(a->C);
+    int caller_dev = 0;
+    cudaGetDevice(&caller_dev);   /* workers switch devices; the caller's is restored */
     int rows_const = 0;
     if (w->kind == RW_I8_GW || w->kind == RW_I4_GW)
         rows_const = rkb_ptr_device(a->a_scale) < 0 ? rkb_rows_const(a->a_scale, M, K / w->group) : 0;
@@ -302,12 +311,16 @@ static int rrun(const rkb_rctx *c, const rkb_rweights *w, int M, const rrun_args
      * on the workers' GPUs nothing host-visible is pending, so the call can
      * return after the launches; rocket_b200_ctx_sync collects the status. */
     const int gw = (w->kind == RW_I8_GW || w->kind == RW_I4_GW);
-    if (!rc && rkb_async_enabled() && !staged && !gw) return 0;
+    if (!rc && rkb_async_enabled() && !staged && !gw) {
+        cudaSetDevice(caller_dev);
+        return 0;
+    }
     for (int t = 0; t < w->nt; t++) {
         if (w->nsub[t] <= 0) continue;
         int fr = rkb_finish(rkb_get(c->fd[t]), who);
         if (!rc) rc = fr;
     }
+    cudaSetDevice(caller_dev);
     return rc;
 }
 

@@ -210,3 +210,45 @@ def test_i8_resident_shard_widths_m4096(rkb, orc, nsub, K):
     # tile edges of the 128- and 256-row tilings, and the ends
     rows = sorted({0, 1, 127, 128, 255, 256, 511, 512, 2047, 2048, 3839, 3840, 4094, 4095})
     assert np.array_equal(C[rows], orc.matmul_int8(A[rows], B, nthreads=8))
+
+
+def _ngpu():
+    import torch
+    return torch.cuda.device_count()
+
+
+@pytest.mark.parametrize("nthreads", [2, 8])
+def test_multi_gpu_workers_match_one(rkb, orc, nthreads):
+    """Workers spread over GPUs (worker t on device t mod count): the resident
+    int8 and fp16 fan-out (rocket_matmul_int8_prepacked, rocket_matmul_fp16_mt)
+    with host and with device A / C is bit-identical to one worker, and the
+    caller's current device is left as it was."""
+    import torch
+    if _ngpu() < 2 or (nthreads == 8 and _ngpu() < 8):
+        pytest.skip(f"needs {min(nthreads, 8)} GPUs")
+    torch.cuda.set_device(0)
+    M, K, N = 256, 1024, 1024
+    A = orc.uniform_i8(71, -128, 127, (M, K))
+    B = orc.uniform_i8(72, -128, 127, (N, K))
+    ref = orc.matmul_int8(A, B, nthreads=8)
+    for nt in (1, nthreads):
+        ctx = rkb.lib.rocket_i8_ctx_create(nt)
+        w = rkb.lib.rocket_i8_weights_pack(ctx, M, K, N, rkb.ptr(B))
+        assert ctx and w
+        C = np.zeros((M, N), np.int32)
+        assert rkb.lib.rocket_matmul_int8_prepacked(ctx, M, K, N, rkb.ptr(A), rkb.ptr(C), w) == 0
+        assert np.array_equal(C, ref), nt
+        dA = torch.from_numpy(A).cuda()
+        dC = torch.zeros((M, N), dtype=torch.int32, device="cuda")
+        assert rkb.lib.rocket_matmul_int8_prepacked(ctx, M, K, N, rkb.ptr(dA), rkb.ptr(dC), w) == 0
+        assert torch.cuda.current_device() == 0
+        assert np.array_equal(dC.cpu().numpy(), ref), nt
+        rkb.lib.rocket_i8_weights_free(ctx, w)
+        rkb.lib.rocket_i8_ctx_free(ctx)
+    Ah = orc.normal_f16(73, 1.0 / 32, (M, K))
+    Bh = orc.normal_f16(74, 1.0, (N, K))
+    C1 = np.zeros((M, N), np.float16)
+    Cn = np.zeros((M, N), np.float16)
+    assert rkb.lib.rocket_matmul_fp16_mt(M, K, N, rkb.ptr(Ah), rkb.ptr(Bh), rkb.ptr(C1), 1) == 0
+    assert rkb.lib.rocket_matmul_fp16_mt(M, K, N, rkb.ptr(Ah), rkb.ptr(Bh), rkb.ptr(Cn), nthreads) == 0
+    assert np.array_equal(C1.view(np.uint16), Cn.view(np.uint16))
