@@ -102,7 +102,7 @@ int rocket_b200_ctx_fd(const void *ctx, int worker)
     return c->fd[worker];
 }
 
-static void rctx_free(rkb_rctx *c)
+static void rctx_free_on(rkb_rctx *c)
 {
     for (int t = 0; t < c->nthreads; t++) rocket_close(c->fd[t]);
 }
@@ -120,7 +120,7 @@ static int nstep(int N, int nthreads, int atom)
  * for a fused N-concatenation).  Existing per-worker buffers large enough are
  * reused (the streaming contexts re-fill every call); finish = 0 leaves the
  * copies queued for the call that follows. */
-static int rweights_fill(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M, int K, int N, int nseg,
+static int rweights_fill_on(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M, int K, int N, int nseg,
                          const void *const *Bs, const int *Ns, int group, int finish, const char *who)
 {
     void *keep[RKB_MAX_WORKERS];
@@ -197,6 +197,36 @@ static int rweights_fill(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M
     return rc;
 }
 
+static void rweights_free_on(const rkb_rctx *c, rkb_rweights *w);
+
+/* The workers switch the current CUDA device; every entry point leaves the
+ * caller's current device as it found it. */
+static int rweights_fill(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M, int K, int N, int nseg,
+                         const void *const *Bs, const int *Ns, int group, int finish, const char *who)
+{
+    int dev0 = 0;
+    cudaGetDevice(&dev0);
+    int rc = rweights_fill_on(c, w, kind, M, K, N, nseg, Bs, Ns, group, finish, who);
+    cudaSetDevice(dev0);
+    return rc;
+}
+
+static void rweights_free(const rkb_rctx *c, rkb_rweights *w)
+{
+    int dev0 = 0;
+    cudaGetDevice(&dev0);
+    rweights_free_on(c, w);
+    cudaSetDevice(dev0);
+}
+
+static void rctx_free(rkb_rctx *c)
+{
+    int dev0 = 0;
+    cudaGetDevice(&dev0);
+    rctx_free_on(c);
+    cudaSetDevice(dev0);
+}
+
 static int rweights_pack(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M, int K, int N,
                          const void *B, int group, const char *who)
 {
@@ -204,14 +234,11 @@ static int rweights_pack(const rkb_rctx *c, rkb_rweights *w, rw_kind kind, int M
     const void *bs[1] = {B};
     const int ns[1] = {N};
     int rc = rweights_fill(c, w, kind, M, K, N, 1, bs, ns, group, 1, who);
-    if (rc) {
-        for (int t = 0; t < c->nthreads; t++)
-            if (w->dev[t]) { rkb_get(c->fd[t]); cudaFree(w->dev[t]); w->dev[t] = NULL; }
-    }
+    if (rc) rweights_free(c, w);
     return rc;
 }
 
-static void rweights_free(const rkb_rctx *c, rkb_rweights *w)
+static void rweights_free_on(const rkb_rctx *c, rkb_rweights *w)
 {
     for (int t = 0; t < c->nthreads; t++) {
         if (!w->dev[t]) continue;
@@ -328,11 +355,13 @@ int rocket_b200_ctx_sync(const void *ctx)
 {
     const rkb_rctx *c = ctx;
     if (!c) return ROCKET_E_SHAPE;
-    int rc = 0;
+    int rc = 0, dev0 = 0;
+    cudaGetDevice(&dev0);
     for (int t = 0; t < c->nthreads; t++) {
         int fr = rkb_finish(rkb_get(c->fd[t]), "rocket_b200_ctx_sync");
         if (!rc) rc = fr;
     }
+    cudaSetDevice(dev0);
     return rc;
 }
 
