@@ -425,7 +425,7 @@ def main_ours(args):
     others = None
     if world == 1 and not args.no_extra:
         others = other_configs(rkb, torch, peaks, derived_peak,
-                               tuple(args.side.split(",")) if args.side else ("c1", "c2", "c3", "c4", "fa"))
+                               tuple(args.side.split(",")) if args.side else ("c1", "c2", "c3", "c4", "ops", "fa"))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -456,7 +456,7 @@ def main_ours(args):
     return 0
 
 
-def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "c4", "fa")):
+def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "c4", "ops", "fa")):
     """fp16 (config 2), W4A8 group-wise (config 3) and int8 latency (config 1)."""
     L = rkb.lib
     out = {}
@@ -547,37 +547,39 @@ def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "
         s3 = torch.cuda.ExternalStream(L.rocket_b200_stream(fd3))
         run3 = lambda: L.rocket_matmul_int4_prepacked_gw(ctx, M, K, N, Aq.data_ptr(), asc.data_ptr(),
                                                          bsc.data_ptr(), Cf.data_ptr(), w)
-        for _ in range(3):
-            run3()
-        torch.cuda.synchronize()
-        # device time per call: calls enqueued back to back, no profiler events
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        L.rocket_b200_set_async(1)
-        a.record(s3)
-        for _ in range(20):
-            run3()
-        b.record(s3)
-        assert L.rocket_b200_ctx_sync(ctx) == 0
-        L.rocket_b200_set_async(0)
-        torch.cuda.synchronize()
-        ms3 = a.elapsed_time(b) / 20
-        # kernel durations: a separate profiled pass
-        L.rocket_b200_profile_reset()
-        L.rocket_b200_profile_enable(1)
-        L.rocket_b200_set_async(1)
-        for _ in range(20):
-            run3()
-        assert L.rocket_b200_ctx_sync(ctx) == 0
-        L.rocket_b200_set_async(0)
-        torch.cuda.synchronize()
-        L.rocket_b200_profile_enable(0)
-        prof = rkb.profile_snapshot()
-        nk, kms = prof.get("wgemm_w4_f16_tcgen05", (1, 0.0))
-        out["config3_w4a8_gw"] = {"tops_call": 2 * M * N * K / ms3 / 1e9, "ms_call": ms3,
-                              "kernel_tops": 2 * M * N * K / (kms / max(nk, 1)) / 1e9,
-                              "kernel_frac_of_measured_f16": 2 * M * N * K / (kms / max(nk, 1)) / 1e9 / peaks["bf16_tflops"],
-                              "per_call_kernels": {k: v for k, v in prof.items() if v[0]},
-                              "note": "fp16 MMA after in-register int4 dequant: peak is the fp16 dense rate"}
+        res3 = {}
+        for mode, mname, fam in ((0, "precise", "wgemm_w4_f16_tcgen05"), (1, "fast", "wgemm_w4_f16_tcgen05")):
+            L.rocket_b200_gw_mode(mode)
+            for _ in range(3):
+                run3()
+            torch.cuda.synchronize()
+            # device time per call: group-wise calls wait for their stream, so
+            # each call's host round trip is inside this figure
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s3)
+            for _ in range(20):
+                run3()
+            b.record(s3)
+            torch.cuda.synchronize()
+            ms3 = a.elapsed_time(b) / 20
+            L.rocket_b200_profile_reset()
+            L.rocket_b200_profile_enable(1)
+            for _ in range(20):
+                run3()
+            torch.cuda.synchronize()
+            L.rocket_b200_profile_enable(0)
+            prof = rkb.profile_snapshot()
+            nk, kms = prof.get(fam, (1, 0.0))
+            res3[mname] = {"tops_call": 2 * M * N * K / ms3 / 1e9, "ms_call": ms3,
+                           "kernel_tops": 2 * M * N * K / (kms / max(nk, 1)) / 1e9,
+                           "kernel_frac_of_measured_f16": 2 * M * N * K / (kms / max(nk, 1)) / 1e9 / peaks["bf16_tflops"],
+                           "per_call_kernels": {k: v for k, v in prof.items() if v[0]}}
+        L.rocket_b200_gw_mode(0)
+        res3["note"] = ("precise (default): exact integer partial per 32-wide group from the fp16 MMA on unscaled "
+                        "operands, scaled and summed in fp32 (the reference's definition, its gates' 1e-5 rms bound); "
+                        "fast: w*scale rounded to fp16 in-register before the MMA (north-star 1e-2 bound). "
+                        "Peak is the fp16 dense rate")
+        out["config3_w4a8_gw"] = res3
         L.rocket_i4_weights_free(ctx, w)
         L.rocket_i4_ctx_free(ctx)
 
@@ -656,6 +658,38 @@ def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "
             "per_kernel_ms": {k: v[1] / 10 for k, v in prof.items() if v[0]},
             "note": "batched over 4 sequences via rocket_b200_encoder_block_batched_fp16"}
 
+    # HBM-bound encoder ops standalone, at sizes above L2 (126 MB): achieved
+    # GB/s = bytes read + written per call / device time per call
+    if "ops" in which:
+        res = {}
+        go = torch.Generator(device="cuda")
+        go.manual_seed(5)
+        SM_R, SM_N = 48000, 1500            # softmax rows of config-4 attention scores (32 heads x 1500)
+        xs = torch.randn((SM_R, SM_N), device="cuda", generator=go).half()
+        ys = torch.empty_like(xs)
+        ms = timed(lambda: L.rocket_softmax_fp16(dev.fd, SM_R, SM_N, xs.data_ptr(), ys.data_ptr()), 50)
+        res["softmax_48000x1500"] = {"us": ms * 1e3, "gbs": 2 * xs.numel() * 2 / (ms / 1e3) / 1e9}
+        del xs, ys
+        NE = 1 << 26
+        xa = torch.randn(NE, device="cuda", generator=go).half()
+        xb = torch.randn(NE, device="cuda", generator=go).half()
+        yo = torch.empty_like(xa)
+        ms = timed(lambda: L.rocket_activation_fp16(dev.fd, 5, xa.data_ptr(), yo.data_ptr(), NE), 50)
+        res["gelu_64Mi"] = {"us": ms * 1e3, "gbs": 2 * NE * 2 / (ms / 1e3) / 1e9}
+        ms = timed(lambda: L.rocket_ew_add_fp16(dev.fd, xa.data_ptr(), xb.data_ptr(), yo.data_ptr(), NE), 50)
+        res["ew_add_64Mi"] = {"us": ms * 1e3, "gbs": 3 * NE * 2 / (ms / 1e3) / 1e9}
+        del xa, xb, yo
+        RN, RH = 100000, 512
+        xr = torch.randn((RN, RH), device="cuda", generator=go).half()
+        gr = torch.ones(RH, device="cuda", dtype=torch.float16)
+        yr = torch.empty_like(xr)
+        ms = timed(lambda: L.rocket_rmsnorm_fp16(dev.fd, RN, RH, xr.data_ptr(), gr.data_ptr(), 1e-6,
+                                                 yr.data_ptr()), 50)
+        res["rmsnorm_100000x512"] = {"us": ms * 1e3, "gbs": 2 * xr.numel() * 2 / (ms / 1e3) / 1e9}
+        for v in res.values():
+            v["frac_of_measured_hbm"] = v["gbs"] / peaks["hbm_gbs"]
+        out["hbm_ops"] = res
+
     # masked grouped-query flash attention (rocket_flash_attn_fp16), Llama-style prefill shapes
     if "fa" in which:
         res = {}
@@ -713,7 +747,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true")
-    ap.add_argument("--side", default="", help="comma list of side configs to run (c1,c2,c3,c4,fa)")
+    ap.add_argument("--side", default="", help="comma list of side configs to run (c1,c2,c3,c4,ops,fa)")
     ap.add_argument("--side-only", action="store_true", help="run only the side configs (profiling)")
     ap.add_argument("--streams", type=int, default=4,
                     help="4: each GEMM of the set on its own context/stream (concurrent); 1: one stream")
@@ -729,7 +763,7 @@ def main():
         rkb = load_pkg()
         peaks, _ = load_peaks()
         res = other_configs(rkb, torch, peaks, 2.0 * peaks.get("bf16_tflops", 1590.0),
-                            tuple(args.side.split(",")) if args.side else ("c1", "c2", "c3", "c4", "fa"))
+                            tuple(args.side.split(",")) if args.side else ("c1", "c2", "c3", "c4", "ops", "fa"))
         print(json.dumps({"side_configs": res}), flush=True)
         return 0
     return main_ours(args)

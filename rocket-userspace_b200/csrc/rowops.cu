@@ -11,6 +11,7 @@
 // storage; reductions are exact-order independent to within fp32 rounding.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
+#include <type_traits>
 #include <stdint.h>
 #include "../src/rkb_kernels.h"
 #include "../../include/rocket_npu.h"
@@ -190,6 +191,73 @@ __global__ void softmax_rows(const __half *__restrict__ x, int M, int N, int mod
             for (int i = lane; i < N; i += 32) {
                 const float v = __half2float(r.p[i]);
                 o[i] = __float2half_rn(mode ? v - lse : expf(v - mx) * inv);
+            }
+        }
+    }
+}
+
+// Softmax / log-softmax with the row held in registers: one HBM read and one
+// write per element, one exponential per element (rows of up to 32 * MAXE
+// halves).  V halves per load (16 / 8 / 4 / 2 bytes), chosen by the caller
+// from N and the pointers' alignment, so odd-sized rows (1500 in the config-4
+// attention) still load whole vectors.  Element e of chunk c of a lane is row
+// index (c * 32 + lane) * V + e; indices past N hold -inf (weight 0).
+template <int V, int MAXE>
+__global__ void __launch_bounds__(128, 4) softmax_rows_reg(const __half *__restrict__ x, int M, int N, int mode,
+                                 __half *__restrict__ out) {
+    constexpr int MAXC = MAXE / V;
+    using Vec = typename std::conditional<V == 8, uint4, typename std::conditional<V == 4, uint2,
+                typename std::conditional<V == 2, uint32_t, uint16_t>::type>::type>::type;
+    const int warps = blockDim.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nch = (N + 32 * V - 1) / (32 * V);
+    for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+        const Vec *src = reinterpret_cast<const Vec *>(x + static_cast<size_t>(row) * N);
+        // all of the row's loads are issued before any is used
+        Vec raw[MAXC];
+#pragma unroll
+        for (int c = 0; c < MAXC; ++c) {
+            const int i = c * 32 + lane;
+            if (c < nch && i * V < N) raw[c] = __ldcs(src + i);
+        }
+        // the row stays as fp16 in registers; the exponential is evaluated
+        // again for the output instead of keeping fp32 copies (half the
+        // registers, so twice the rows in flight per SM)
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < MAXC; ++c) {
+            const bool in = c < nch && (c * 32 + lane) * V < N;
+            const __half *h = reinterpret_cast<const __half *>(&raw[c]);
+#pragma unroll
+            for (int e = 0; e < V; ++e)
+                if (in) mx = fmaxf(mx, __half2float(h[e]));
+        }
+        mx = warp_max(mx);
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < MAXC; ++c) {
+            const bool in = c < nch && (c * 32 + lane) * V < N;
+            const __half *h = reinterpret_cast<const __half *>(&raw[c]);
+#pragma unroll
+            for (int e = 0; e < V; ++e)
+                if (in) sum += __expf(__half2float(h[e]) - mx);
+        }
+        sum = warp_sum(sum);
+        const float inv = 1.f / sum, lse = mx + __logf(sum);
+        Vec *dst = reinterpret_cast<Vec *>(out + static_cast<size_t>(row) * N);
+#pragma unroll
+        for (int c = 0; c < MAXC; ++c) {
+            const int i = c * 32 + lane;
+            if (c < nch && i * V < N) {
+                const __half *h = reinterpret_cast<const __half *>(&raw[c]);
+                Vec w;
+                __half *wh = reinterpret_cast<__half *>(&w);
+#pragma unroll
+                for (int e = 0; e < V; ++e) {
+                    const float xv = __half2float(h[e]);
+                    wh[e] = __float2half_rn(mode ? xv - lse : __expf(xv - mx) * inv);
+                }
+                __stcs(dst + i, w);
             }
         }
     }
@@ -398,6 +466,32 @@ int rkb_softmax_rows(const void *x, int M, int N, int log_mode, void *out, cudaS
     const int warps = 8;
     int grid = (M + warps - 1) / warps;
     if (grid > 148 * 16) grid = 148 * 16;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out);
+    const __half *hx = static_cast<const __half *>(x);
+    __half *ho = static_cast<__half *>(out);
+    const int m = log_mode ? 1 : 0;
+    if (N <= 32 * 64) {
+        const int v = (N % 8 == 0 && (al & 15) == 0) ? 8 : (N % 4 == 0 && (al & 7) == 0) ? 4
+                    : (N % 2 == 0 && (al & 3) == 0) ? 2 : 1;
+        // per-lane row share, rounded to the next instantiated size (whole V-vectors)
+        const int need = ((N + 32 * v - 1) / (32 * v)) * v;
+        const int e = need <= 8 ? 8 : need <= 16 ? 16 : need <= 32 ? 32 : need <= 48 ? 48 : 64;
+        // 4-warp blocks: finer occupancy steps for these register-heavy rows
+        int grid4 = (M + 3) / 4;
+        if (grid4 > 148 * 32) grid4 = 148 * 32;
+        const dim3 gr(grid4), bl(128);
+#define RKB_SMX(V, E) softmax_rows_reg<V, E><<<gr, bl, 0, s>>>(hx, M, N, m, ho)
+#define RKB_SMX_E(V) do { if (e == 8) RKB_SMX(V, 8); else if (e == 16) RKB_SMX(V, 16); \
+                          else if (e == 32) RKB_SMX(V, 32); else if (e == 48) RKB_SMX(V, 48); \
+                          else RKB_SMX(V, 64); } while (0)
+        if (v == 8) RKB_SMX_E(8);
+        else if (v == 4) RKB_SMX_E(4);
+        else if (v == 2) RKB_SMX_E(2);
+        else RKB_SMX_E(1);
+#undef RKB_SMX_E
+#undef RKB_SMX
+        return status();
+    }
     softmax_rows<<<grid, warps * 32, 0, s>>>(static_cast<const __half *>(x), M, N, log_mode ? 1 : 0,
                                              static_cast<__half *>(out));
     return status();
