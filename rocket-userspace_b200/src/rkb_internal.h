@@ -40,6 +40,14 @@ typedef struct rkb_handle {
     void *scr[RKB_NSCR];
     size_t scr_cap[RKB_NSCR];
     struct { void *dptr; void *hptr; size_t size; int live; } bo[RKB_MAX_BOS];
+    /* pinned bounce buffers for small pageable host operands (grow-only), the
+     * event after each one's last copy, and host copies-out that complete in
+     * rkb_finish */
+    void *pin[RKB_NSCR + 1];
+    size_t pin_cap[RKB_NSCR + 1];
+    cudaEvent_t pin_ev[RKB_NSCR + 1];
+    struct { void *user; const void *pin; size_t bytes; } pend;
+    int npend;
     /* profiler: event pairs recorded around launches, drained in rkb_finish */
     cudaEvent_t ev[RKB_PROF_SLOTS][2];
     int ev_fam[RKB_PROF_SLOTS];

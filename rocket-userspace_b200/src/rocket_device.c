@@ -200,6 +200,10 @@ void rocket_close(int fd)
     if (!h) return;
     cudaStreamSynchronize(h->stream);
     for (int i = 0; i < RKB_NSCR; i++) cudaFree(h->scr[i]);
+    for (int i = 0; i <= RKB_NSCR; i++) {
+        if (h->pin[i]) cudaFreeHost(h->pin[i]);
+        if (h->pin_ev[i]) cudaEventDestroy(h->pin_ev[i]);
+    }
     for (int i = 0; i < RKB_MAX_BOS; i++)
         if (h->bo[i].live) { cudaFree(h->bo[i].dptr); cudaFreeHost(h->bo[i].hptr); }
     for (int i = 0; i < h->ev_made; i++) {
@@ -232,26 +236,71 @@ void *rkb_scratch(rkb_handle *h, int slot, size_t bytes)
     return h->scr[slot];
 }
 
-int rkb_ptr_device(const void *p)
+/* CUDA device owning p; -1 for pinned (or otherwise CUDA-known) host memory,
+ * -2 for pageable host memory. */
+static int ptr_kind(const void *p)
 {
     struct cudaPointerAttributes a;
     if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
         cudaGetLastError();
-        return -1;
+        return -2;
     }
     if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) return a.device;
-    return -1;
+    return a.type == cudaMemoryTypeUnregistered ? -2 : -1;
+}
+
+int rkb_ptr_device(const void *p)
+{
+    const int k = ptr_kind(p);
+    return k >= 0 ? k : -1;
+}
+
+/* Pageable operands up to this size go through a pinned bounce buffer: one
+ * host memcpy plus an asynchronous DMA instead of the driver's synchronous
+ * staging of pageable memory.  Larger ones are copied directly. */
+#define RKB_BOUNCE_MAX ((size_t)8 << 20)
+
+/* Pinned buffer `slot` of at least `bytes`, free of queued copies. */
+static void *pin_slot(rkb_handle *h, int slot, size_t bytes)
+{
+    if (h->pin_ev[slot]) cudaEventSynchronize(h->pin_ev[slot]);
+    if (h->pin_cap[slot] < bytes) {
+        if (h->pin[slot]) cudaFreeHost(h->pin[slot]);
+        h->pin[slot] = NULL;
+        h->pin_cap[slot] = 0;
+        size_t cap = (bytes + 0xFFFF) & ~(size_t)0xFFFF;
+        if (cudaHostAlloc(&h->pin[slot], cap, cudaHostAllocDefault) != cudaSuccess) {
+            cudaGetLastError();
+            return NULL;
+        }
+        h->pin_cap[slot] = cap;
+    }
+    if (!h->pin_ev[slot] &&
+        cudaEventCreateWithFlags(&h->pin_ev[slot], cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        h->pin_ev[slot] = NULL;
+        return NULL;
+    }
+    return h->pin[slot];
 }
 
 const void *rkb_stage_in(rkb_handle *h, int slot, const void *user, size_t bytes)
 {
-    if (rkb_ptr_device(user) == h->device && ((uintptr_t)user & 15) == 0) return user;
+    const int kind = ptr_kind(user);
+    if (kind == h->device && ((uintptr_t)user & 15) == 0) return user;
     void *d = rkb_scratch(h, slot, bytes);
     if (!d) return NULL;
-    if (cudaMemcpyAsync(d, user, bytes, cudaMemcpyDefault, h->stream) != cudaSuccess) {
+    const void *src = user;
+    void *p = (kind == -2 && bytes <= RKB_BOUNCE_MAX) ? pin_slot(h, slot, bytes) : NULL;
+    if (p) {
+        memcpy(p, user, bytes);
+        src = p;
+    }
+    if (cudaMemcpyAsync(d, src, bytes, cudaMemcpyDefault, h->stream) != cudaSuccess) {
         ROCKET_LOGE("rkb: input copy failed: %s\n", cudaGetErrorString(cudaGetLastError()));
         return NULL;
     }
+    if (p) cudaEventRecord(h->pin_ev[slot], h->stream);
     return d;
 }
 
@@ -268,6 +317,20 @@ void *rkb_stage_out(rkb_handle *h, int slot, void *user, size_t bytes, int *copy
 int rkb_stage_out_finish(rkb_handle *h, void *user, const void *dev, size_t bytes, int copy_back)
 {
     if (!copy_back) return 0;
+    /* a small pageable output lands in the pinned bounce buffer and is copied
+     * out by rkb_finish once the stream is done (one output per wait) */
+    if (h->npend == 0 && bytes <= RKB_BOUNCE_MAX && ptr_kind(user) == -2) {
+        void *p = pin_slot(h, RKB_NSCR, bytes);
+        if (p && cudaMemcpyAsync(p, dev, bytes, cudaMemcpyDeviceToHost, h->stream) == cudaSuccess) {
+            cudaEventRecord(h->pin_ev[RKB_NSCR], h->stream);
+            h->pend.user = user;
+            h->pend.pin = p;
+            h->pend.bytes = bytes;
+            h->npend = 1;
+            return 0;
+        }
+        cudaGetLastError();
+    }
     if (cudaMemcpyAsync(user, dev, bytes, cudaMemcpyDefault, h->stream) != cudaSuccess) {
         ROCKET_LOGE("rkb: output copy failed: %s\n", cudaGetErrorString(cudaGetLastError()));
         return ROCKET_E_DEVICE;
@@ -305,6 +368,9 @@ int rkb_finish(rkb_handle *h, const char *who)
 {
     uint64_t to = (uint64_t)rkb_env_long("ROCKET_WAIT_MS", 8000) * 1000000ull;
     int rc = wait_stream(h, to);
+    const int npend = h->npend;
+    h->npend = 0;
+    if (rc == 0 && npend) memcpy(h->pend.user, h->pend.pin, h->pend.bytes);
     if (rc == -EBUSY) {
         ROCKET_LOGE("%s: WAIT TIMEOUT after %llu ms\n", who, (unsigned long long)(to / 1000000ull));
         return ROCKET_E_DEVICE;
