@@ -8,19 +8,24 @@
 // is the fp64 host loop at src/rocket_attn.c:41-84.
 //
 // One CTA = 128 queries of one (batch, head); head_dim 64.  Roles:
-//   warp 0      TMA: Q once; K and V^T blocks of 128 keys into a 2-deep ring
+//   warp 0      TMA: Q once; K blocks of 128 keys into a 2-deep ring, V^T
+//               blocks into one buffer (two CTAs fit on an SM)
 //   warp 1      MMA issuer: S_j = Q K_j^T (M=128, N=128, fp32 in TMEM cols
 //               0..127), O_j = P_j V_j (M=128, N=64, TMEM cols 128..191); S_{j+1}
 //               is issued as soon as S_j has been read, so it overlaps the
 //               softmax of block j
 //   warps 2..9  softmax, two warps per TMEM lane quarter: each thread owns one
-//               query row and half of every 128-key block; the pair exchanges
-//               half-block row maxima through shared memory (an mbarrier with
-//               a bounded wait), then each computes exp2 weights and its part
-//               of the row sum in fp32, writes its 64-key panel of P_j as fp16
-//               into the 128-byte-swizzled shared tile for the P V MMA, and
-//               folds its 32 columns of O_{j-1} from TMEM into registers; the
+//               query row and half of every 128-key block; it reads its 64
+//               scores from TMEM twice, 32 at a time (row max, then weights),
+//               exchanges half-block row maxima with its partner through
+//               shared memory (an mbarrier with a bounded wait), computes exp2
+//               weights and its part of the row sum in fp32, rescales its 32
+//               columns of O in TMEM when the row's reference max moved by
+//               more than 2^8, and writes its 64-key panel of P_j as fp16
+//               into the 128-byte-swizzled shared tile for the P V MMA; the
 //               two partial row sums are added at the end
+// About 100 KB of shared memory, 256 TMEM columns and 85 registers a thread,
+// so two CTAs share an SM.
 // Keys past T (the last block) are masked to -inf.  Inputs come from
 // rkb_split_heads: Q, K [B*H, Tp, 64] and V^T [B*H, 64, Tp], zero-padded.
 #include <cuda.h>
@@ -44,16 +49,18 @@ constexpr int Q_BYTES = BQ * DH * 2;        // 16 KB
 constexpr int K_BYTES = BKV * DH * 2;       // 16 KB
 constexpr int VT_BYTES = DH * BKV * 2;      // 16 KB (two 64-key panels of 8 KB)
 constexpr int P_BYTES = BQ * BKV * 2;       // 32 KB (two 64-key panels of 16 KB)
-constexpr int KV_STAGES = 2;
-constexpr int KV_STAGE = K_BYTES + VT_BYTES;
+// Shared memory fits two CTAs per SM (~98 KB each): K in a 2-deep ring (K_{j+1}
+// is needed as soon as S_j has been read), V^T and P single-buffered (V_j is
+// read only by P_j V_j, which runs a whole softmax step after S_j).
+constexpr int K_STAGES = 2;
 constexpr int OFF_Q = 0;
-constexpr int OFF_KV = Q_BYTES;
-constexpr int OFF_P = OFF_KV + KV_STAGES * KV_STAGE;
-constexpr int P_BUFS = 2;                     // P double-buffered: softmax j+1 overlaps P_j V_j
-constexpr int OFF_X = OFF_P + P_BUFS * P_BYTES;   // row-max exchange [2 parities][2 halves][128] + sums [2][128]
-constexpr int X_BYTES = (2 * 2 * BQ + 2 * BQ) * 4;
+constexpr int OFF_K = Q_BYTES;
+constexpr int OFF_V = OFF_K + K_STAGES * K_BYTES;
+constexpr int OFF_P = OFF_V + VT_BYTES;
+constexpr int OFF_X = OFF_P + P_BYTES;        // row-max exchange [2 parities][2 halves][128]; the
+constexpr int X_BYTES = 2 * 2 * BQ * 4;       // final row sums reuse the parity not read last
 constexpr int OFF_BAR = OFF_X + X_BYTES;
-constexpr int NBARS = 1 + 2 * KV_STAGES + 5 + 8;
+constexpr int NBARS = 1 + 2 * K_STAGES + 2 + 5 + 8;
 constexpr float RESCALE_LOG2 = 8.f;    // the reference max moves only when a row's max grows by > 2^8
 constexpr int SMEM = OFF_BAR + NBARS * 8 + 16 + 1024;
 constexpr uint32_t TMEM_COLS = 256;
@@ -81,7 +88,7 @@ struct Args {
     int *err;
 };
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(NUM_THREADS, 2)
 attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmVt, const Args g) {
     extern __shared__ uint8_t smem_raw[];
@@ -91,8 +98,11 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBARS);
     const uint32_t q_full = smem_u32(&bars[0]);
-    auto kv_full = [&](int s) { return smem_u32(&bars[1 + s]); };
-    auto kv_empty = [&](int s) { return smem_u32(&bars[1 + KV_STAGES + s]); };
+    auto k_full = [&](int s) { return smem_u32(&bars[1 + s]); };
+    auto k_empty = [&](int s) { return smem_u32(&bars[1 + K_STAGES + s]); };
+    const uint32_t v_full = smem_u32(&bars[1 + 2 * K_STAGES]);
+    const uint32_t v_empty = smem_u32(&bars[2 + 2 * K_STAGES]);
+    constexpr int KV_STAGES = K_STAGES + 1;   // offsets of the barriers below
     const uint32_t s_full = smem_u32(&bars[1 + 2 * KV_STAGES]);
     const uint32_t s_free = smem_u32(&bars[2 + 2 * KV_STAGES]);
     const uint32_t p_full = smem_u32(&bars[3 + 2 * KV_STAGES]);
@@ -103,8 +113,8 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     // half-block row maxima (every block) and their row sums (at the end)
     auto xmax_bar = [&](int q) { return smem_u32(&bars[6 + 2 * KV_STAGES + q]); };
     auto xsum_bar = [&](int q) { return smem_u32(&bars[10 + 2 * KV_STAGES + q]); };
-    auto sK = [&](int s) { return sb + OFF_KV + s * KV_STAGE; };
-    auto sVt = [&](int s) { return sb + OFF_KV + s * KV_STAGE + K_BYTES; };
+    auto sK = [&](int s) { return sb + OFF_K + s * K_BYTES; };
+    const uint32_t sVt = sb + OFF_V;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = blockIdx.x, bh = blockIdx.y;
@@ -114,10 +124,12 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmVt);
         mbar_init(q_full, 1);
-        for (int s = 0; s < KV_STAGES; ++s) {
-            mbar_init(kv_full(s), 1);
-            mbar_init(kv_empty(s), 1);
+        for (int s = 0; s < K_STAGES; ++s) {
+            mbar_init(k_full(s), 1);
+            mbar_init(k_empty(s), 1);
         }
+        mbar_init(v_full, 1);
+        mbar_init(v_empty, 1);
         mbar_init(s_full, 1);
         mbar_init(s_free, 8);
         mbar_init(p_full, 8);
@@ -143,14 +155,21 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         if (lane == 0) {
             mbar_arrive_expect_tx(q_full, Q_BYTES);
             tma_load_2d(sb + OFF_Q, &tmQ, 0, bh * g.Tp + qt * BQ, q_full);
-            for (int j = 0; j < nkb; ++j) {
-                const int s = j % KV_STAGES;
-                const uint32_t ph = (j / KV_STAGES) & 1;
-                if (!mbar_wait(kv_empty(s), ph ^ 1, g.err, ERR_WAIT_PRODUCER)) break;
-                mbar_arrive_expect_tx(kv_full(s), KV_STAGE);
-                tma_load_2d(sK(s), &tmK, 0, bh * g.Tp + j * BKV, kv_full(s));
-                tma_load_2d(sVt(s), &tmVt, j * BKV, bh * DH, kv_full(s));
-                tma_load_2d(sVt(s) + VT_BYTES / 2, &tmVt, j * BKV + 64, bh * DH, kv_full(s));
+            // order: K_0, then K_{j+1} ahead of V_j (V_j waits for P_{j-1} V_{j-1})
+            auto load_k = [&](int j) {
+                const int s = j % K_STAGES;
+                if (!mbar_wait(k_empty(s), ((j / K_STAGES) & 1) ^ 1, g.err, ERR_WAIT_PRODUCER)) return false;
+                mbar_arrive_expect_tx(k_full(s), K_BYTES);
+                tma_load_2d(sK(s), &tmK, 0, bh * g.Tp + j * BKV, k_full(s));
+                return true;
+            };
+            bool ok = nkb > 0 && load_k(0);
+            for (int j = 0; j < nkb && ok; ++j) {
+                if (j + 1 < nkb && !load_k(j + 1)) break;
+                if (!mbar_wait(v_empty, (j & 1) ^ 1, g.err, ERR_WAIT_PRODUCER)) break;
+                mbar_arrive_expect_tx(v_full, VT_BYTES);
+                tma_load_2d(sVt, &tmVt, j * BKV, bh * DH, v_full);
+                tma_load_2d(sVt + VT_BYTES / 2, &tmVt, j * BKV + 64, bh * DH, v_full);
             }
         }
     } else if (warp == 1) {
@@ -158,37 +177,39 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             constexpr uint32_t IDS = idesc_f16_f32acc(BQ, BKV);
             constexpr uint32_t IDO = idesc_f16_f32acc(BQ, DH);
             bool ok = mbar_wait(q_full, 0, g.err, ERR_WAIT_MMA_FULL) &&
-                      mbar_wait(kv_full(0), 0, g.err, ERR_WAIT_MMA_FULL);
+                      mbar_wait(k_full(0), 0, g.err, ERR_WAIT_MMA_FULL);
             if (ok) {
                 tc_fence_after();
                 const uint64_t qd = smem_desc_sw128(sb + OFF_Q), kd = smem_desc_sw128(sK(0));
 #pragma unroll
                 for (int k = 0; k < 4; ++k) tc_mma_f16(tmem + S_COL, qd + 2 * k, kd + 2 * k, IDS, k > 0);
                 tc_commit(s_full);
+                tc_commit(k_empty(0));
             }
             for (int j = 0; j < nkb && ok; ++j) {
                 if (j + 1 < nkb) {
-                    const int s1 = (j + 1) % KV_STAGES;
-                    if (!mbar_wait(kv_full(s1), ((j + 1) / KV_STAGES) & 1, g.err, ERR_WAIT_MMA_FULL) ||
+                    const int s1 = (j + 1) % K_STAGES;
+                    if (!mbar_wait(k_full(s1), ((j + 1) / K_STAGES) & 1, g.err, ERR_WAIT_MMA_FULL) ||
                         !mbar_wait(s_free, j & 1, g.err, ERR_WAIT_MMA_ACC)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t qd = smem_desc_sw128(sb + OFF_Q), kd = smem_desc_sw128(sK(s1));
 #pragma unroll
                     for (int k = 0; k < 4; ++k) tc_mma_f16(tmem + S_COL, qd + 2 * k, kd + 2 * k, IDS, k > 0);
                     tc_commit(s_full);
+                    tc_commit(k_empty(s1));
                 }
-                if (!mbar_wait(p_full, j & 1, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
+                if (!mbar_wait(p_full, j & 1, g.err, ERR_WAIT_MMA_FULL) ||
+                    !mbar_wait(v_full, j & 1, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
                 tc_fence_after();
-                const int s = j % KV_STAGES;
-                const uint32_t pbuf = sb + OFF_P + (j & 1) * P_BYTES;
+                const uint32_t pbuf = sb + OFF_P;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint64_t pd = smem_desc_sw128(pbuf + (kk >> 2) * (P_BYTES / 2) + (kk & 3) * 32);
-                    const uint64_t vd = smem_desc_sw128(sVt(s) + (kk >> 2) * (VT_BYTES / 2) + (kk & 3) * 32);
+                    const uint64_t vd = smem_desc_sw128(sVt + (kk >> 2) * (VT_BYTES / 2) + (kk & 3) * 32);
                     tc_mma_f16(tmem + O_COL, pd, vd, IDO, (j | kk) != 0);   // O accumulates in TMEM
                 }
                 tc_commit(pv_done(j & 1));
-                tc_commit(kv_empty(s));
+                tc_commit(v_empty);
             }
             if (!ok) {
                 tc_commit(q_full);   // drain: arrives once every issued MMA has finished
@@ -204,7 +225,6 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const int row = q4 * 32 + lane;
         const uint32_t tl = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
         float *xm = reinterpret_cast<float *>(smem + OFF_X);        // [parity][half][row]
-        float *xs = xm + 2 * 2 * BQ;                                // [half][row]
         constexpr int HK = BKV / 2;                                 // keys per warp per block
         constexpr int HD = DH / 2;                                  // output columns per warp
         float m = -INFINITY, l = 0.f;
@@ -212,29 +232,23 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         for (int j = 0; j < nkb; ++j) {
             if (!mbar_wait_warp(s_full, j & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
             tc_fence_after();
-            float sv[HK];
+            // the scores stay in TMEM and are read twice, 32 at a time (max, then
+            // weights), which keeps the thread within the register budget of
+            // two CTAs per SM.  The scale (> 0) is folded into the exponent:
+            // max over raw scores, weights ex2(s * scale_log2 - m); keys past T
+            // exist only in the last block.
+            const int kbase = j * BKV + half * HK;
+            const bool tail = j * BKV + BKV > g.T;
+            float mr = -INFINITY;
 #pragma unroll
             for (int c = 0; c < HK; c += 32) {
                 uint32_t r[32];
                 tmem_ld32(tl + S_COL + half * HK + c, r);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) sv[c + i] = __uint_as_float(r[i]);
+                for (int i = 0; i < 32; ++i)
+                    if (!tail || kbase + c + i < g.T) mr = fmaxf(mr, __uint_as_float(r[i]));
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_free);
-            // the scale (> 0) is folded into the exponent: max over raw scores,
-            // weights ex2(s * scale_log2 - m); keys past T exist only in the last block
-            const int kbase = j * BKV + half * HK;
-            if (j * BKV + BKV > g.T) {
-#pragma unroll
-                for (int c = 0; c < HK; ++c)
-                    if (kbase + c >= g.T) sv[c] = -INFINITY;
-            }
-            float mr = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < HK; ++c) mr = fmaxf(mr, sv[c]);
             // exchange half-block maxima with the partner warp (bounded wait)
             xm[((j & 1) * 2 + half) * BQ + row] = mr;
             mbar_arrive(xmax_bar(q4));
@@ -243,20 +257,16 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             // lazy rescale: keep the reference max unless this block exceeds it by 2^8
             const float m_new = mr > m + RESCALE_LOG2 ? mr : m;
             const float alpha = m_new == m ? 1.f : ex2_approx(m - m_new);   // 0 on the first block
-            float sum = 0.f;
-#pragma unroll
-            for (int c = 0; c < HK; ++c) {
-                sv[c] = ex2_approx(fmaf(sv[c], g.scale_log2, -m_new));
-                sum += sv[c];
+            // P_{j-1} V_{j-1} has read the single P buffer and written O
+            if (j > 0 && !mbar_wait_warp(pv_done((j - 1) & 1), ((j - 1) >> 1) & 1, g.err, ERR_WAIT_EPILOGUE)) {
+                ok = false;
+                break;
             }
-            l = l * alpha + sum;                      // this warp's half of the row sum
-            m = m_new;
+            tc_fence_after();
             // O (in TMEM) holds P_0..P_{j-1} V: rescale this warp's 32 columns in
             // place when a row's reference max moved (both warps of the pair see
             // the same rows, so they decide alike)
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-                if (!mbar_wait_warp(pv_done((j - 1) & 1), ((j - 1) >> 1) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
-                tc_fence_after();
                 uint32_t r[32];
                 tmem_ld32(tl + O_COL + half * HD, r);
                 tmem_ld_wait();
@@ -265,24 +275,42 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                 tmem_st32(tl + O_COL + half * HD, r);
                 tmem_st_wait();
             }
-            // P buffer j & 1 was last read by P_{j-2} V_{j-2}
-            if (j >= 2 && !mbar_wait_warp(pv_done(j & 1), ((j >> 1) - 1) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
             // P_j as fp16: this warp's 64 keys are panel `half` of the swizzled A tile
-            uint8_t *prow = smem + OFF_P + (j & 1) * P_BYTES + half * (P_BYTES / 2) + row * 128;
+            uint8_t *prow = smem + OFF_P + half * (P_BYTES / 2) + row * 128;
+            float sum = 0.f;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint32_t hv[4];
+            for (int cc = 0; cc < HK; cc += 32) {
+                uint32_t r[32];
+                tmem_ld32(tl + S_COL + half * HK + cc, r);
+                tmem_ld_wait();
+                float pv[32];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    __half2 p = __floats2half2_rn(sv[c * 8 + 2 * i], sv[c * 8 + 2 * i + 1]);
-                    hv[i] = *reinterpret_cast<uint32_t *>(&p);
+                for (int i = 0; i < 32; ++i) {
+                    const float sv = (!tail || kbase + cc + i < g.T) ? __uint_as_float(r[i]) : -INFINITY;
+                    pv[i] = ex2_approx(fmaf(sv, g.scale_log2, -m_new));
+                    sum += pv[i];
                 }
-                *reinterpret_cast<uint4 *>(prow + ((c ^ (row & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t hv[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        __half2 p = __floats2half2_rn(pv[c * 8 + 2 * i], pv[c * 8 + 2 * i + 1]);
+                        hv[i] = *reinterpret_cast<uint32_t *>(&p);
+                    }
+                    const int ch = cc / 8 + c;
+                    *reinterpret_cast<uint4 *>(prow + ((ch ^ (row & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                }
             }
+            l = l * alpha + sum;                      // this warp's half of the row sum
+            m = m_new;
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) {
+                mbar_arrive(s_free);                  // S_j fully read: S_{j+1} may overwrite it
+                mbar_arrive(p_full);
+            }
         }
         if (ok && nkb > 0 &&
             mbar_wait_warp(pv_done((nkb - 1) & 1), ((nkb - 1) >> 1) & 1, g.err, ERR_WAIT_EPILOGUE)) {
@@ -290,7 +318,9 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             uint32_t r[32];
             tmem_ld32(tl + O_COL + half * HD, r);
             tmem_ld_wait();
-            // the row sum is the two halves' sum (a + b == b + a: both warps agree)
+            // the row sum is the two halves' sum (a + b == b + a: both warps agree);
+            // exchanged through the max-exchange slots of the parity not read last
+            float *xs = xm + (nkb & 1) * 2 * BQ;          // [half][row]
             xs[half * BQ + row] = l;
             mbar_arrive(xsum_bar(q4));
             if (mbar_wait_warp(xsum_bar(q4), 0, g.err, ERR_WAIT_EPILOGUE)) {
@@ -336,6 +366,7 @@ extern "C" int rkb_attention(const void *Q, const void *K, const void *Vt, int B
     cudaGetDevice(&dev);
     std::call_once(once[dev & 15], [] {
         cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        cudaFuncSetAttribute(attn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     });
     CUtensorMap tq, tk, tv;
     const long BH = static_cast<long>(B) * H;
