@@ -681,7 +681,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
             }
         }
     } else if (warp == 1) {
-        if (lane == 0 && leader) {
+        // the whole warp runs the issue loop (warp-uniform addresses and
+        // descriptors); one elected lane issues each tcgen05 instruction
+        if (leader) {
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
@@ -692,36 +694,41 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
             for (; ok && units_next(g, mn_tiles, ui, un); ++it) {
                 const int b = it & 1;
                 const uint32_t aph = (it >> 1) & 1;
-                if (!mbar_wait(tempty_bar(b), aph ^ 1, g.err, ERR_WAIT_MMA_ACC)) { ok = false; break; }
+                if (!mbar_wait_warp(tempty_bar(b), aph ^ 1, g.err, ERR_WAIT_MMA_ACC)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t dcol = tmem_base + b * BN;
                 const int kb0 = un.k0, kb1 = un.k1;
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait(full_bar(s), ph, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
+                    if (!mbar_wait_warp(full_bar(s), ph, g.err, ERR_WAIT_MMA_FULL)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t adesc = smem_desc_sw128(sA(s));
                     const uint64_t bdesc = smem_desc_sw128(sB(s));
+                    if (elect_one()) {
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const uint64_t koff = static_cast<uint64_t>((k * 32) >> 4);
-                        const uint32_t acc = (kb != kb0) || (k != 0);
-                        if (KIND == RKB_IN_I8)        tc_mma_i8_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
-                        else if (KIND == RKB_IN_TF32) tc_mma_tf32_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
-                        else                          tc_mma_f16_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                        for (int k = 0; k < 4; ++k) {
+                            const uint64_t koff = static_cast<uint64_t>((k * 32) >> 4);
+                            const uint32_t acc = (kb != kb0) || (k != 0);
+                            if (KIND == RKB_IN_I8)        tc_mma_i8_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                            else if (KIND == RKB_IN_TF32) tc_mma_tf32_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                            else                          tc_mma_f16_pair(dcol, adesc + koff, bdesc + koff, IDESC, acc);
+                        }
+                        tc_commit_pair(empty_bar(s));
+                        tc_commit_pair(mapa_shared(empty_bar(s), peer));
                     }
-                    tc_commit_pair(empty_bar(s));
-                    tc_commit_pair(mapa_shared(empty_bar(s), peer));
+                    __syncwarp();
                     if (++s == STAGES) { s = 0; ph ^= 1; }
                 }
-                if (ok) {
+                if (ok && elect_one()) {
                     tc_commit_pair(tfull_bar(b));
                     tc_commit_pair(mapa_shared(tfull_bar(b), peer));
                 }
+                __syncwarp();
             }
-            if (!ok) {
+            if (!ok && elect_one()) {
                 tc_commit_pair(drain_bar);
                 mbar_wait_drain(drain_bar, 0);
             }
+            __syncwarp();
         }
     } else {
         const int e = warp - 2;                  // epilogue warp 0..7

@@ -53,6 +53,20 @@ RKB_DEV float ex2_approx(float x) {
     return y;
 }
 
+// One lane of a converged warp (the lowest active one); the same on every
+// lane of the warp.  Lets a whole warp run an MMA-issuing loop (so the
+// loop's addresses and descriptors stay warp-uniform) while exactly one
+// thread issues each tcgen05 instruction.
+RKB_DEV bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(pred));
+    return pred != 0;
+}
+
 // ---- mbarriers -------------------------------------------------------------
 RKB_DEV void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

@@ -358,6 +358,44 @@ __global__ void split_heads(const __half *__restrict__ qkv, long ld, int B, int 
     }
 }
 
+// The same split, one CTA per (64-token tile, batch x head): Q and K rows are
+// copied with 16-byte loads and stores, and V goes through shared memory so
+// that every V^T row segment (64 tokens = 128 bytes) is written with 16-byte
+// stores instead of scattered 2-byte ones.  Tp % 64 == 0, dh % 8 == 0, dh <= 256.
+__global__ void __launch_bounds__(256) split_heads_tiled(const __half *__restrict__ qkv, long ld, int T,
+                                                         int Tp, int H, int dh, __half *__restrict__ Q,
+                                                         __half *__restrict__ K, __half *__restrict__ Vt) {
+    extern __shared__ __align__(16) __half sv[];           // [64 tokens][dh + 8]
+    const int pitch = dh + 8;                                // 16-byte shift per row: fewer bank conflicts
+    const int t0 = blockIdx.x * 64, bh = blockIdx.y;
+    const int b = bh / H, h = bh % H;
+    const int cpr = dh / 8, d = H * dh;
+    for (int i = threadIdx.x; i < 64 * cpr; i += blockDim.x) {
+        const int tl = i / cpr, c = i % cpr, t = t0 + tl;
+        uint4 q = make_uint4(0, 0, 0, 0), k = q, v = q;
+        if (t < T) {
+            const __half *row = qkv + static_cast<size_t>(b * T + t) * ld + h * dh + c * 8;
+            q = *reinterpret_cast<const uint4 *>(row);
+            k = *reinterpret_cast<const uint4 *>(row + d);
+            v = *reinterpret_cast<const uint4 *>(row + 2 * d);
+        }
+        const size_t qo = (static_cast<size_t>(bh) * Tp + t) * dh + c * 8;
+        *reinterpret_cast<uint4 *>(Q + qo) = q;
+        *reinterpret_cast<uint4 *>(K + qo) = k;
+        *reinterpret_cast<uint4 *>(sv + tl * pitch + c * 8) = v;
+    }
+    __syncthreads();
+    __half *vt = Vt + static_cast<size_t>(bh) * dh * Tp + t0;
+    for (int i = threadIdx.x; i < dh * 8; i += blockDim.x) {
+        const int dd = i / 8, tc = i % 8;                    // feature row, 8-token chunk
+        uint4 w;
+        __half *wh = reinterpret_cast<__half *>(&w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wh[j] = sv[(tc * 8 + j) * pitch + dd];
+        *reinterpret_cast<uint4 *>(vt + static_cast<size_t>(dd) * Tp + tc * 8) = w;
+    }
+}
+
 // out[m] = sum (or mean) of row m, fp32 (src/rocket_reduce.c:380-390 definition)
 __global__ void reduce_rows(const __half *__restrict__ x, int M, int H, int mean, float *__restrict__ out) {
     const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
@@ -560,6 +598,16 @@ int rkb_cross_entropy_rows(const void *x, const int *target, int M, int N, float
 int rkb_split_heads(const void *qkv, long ld, int B, int T, int Tp, int H, int dh, void *Q, void *K,
                     void *Vt, cudaStream_t s) {
     if (dh % 8 || (ld % 8)) return ROCKET_E_SHAPE;
+    if (Tp % 64 == 0 && dh <= 256 && (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 &&
+        static_cast<long>(B) * H <= 65535) {
+        const size_t smem = 64 * static_cast<size_t>(dh + 8) * 2;
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(split_heads_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        split_heads_tiled<<<dim3(Tp / 64, B * H), 256, smem, s>>>(
+            static_cast<const __half *>(qkv), ld, T, Tp, H, dh, static_cast<__half *>(Q),
+            static_cast<__half *>(K), static_cast<__half *>(Vt));
+        return status();
+    }
     const size_t total = static_cast<size_t>(B) * H * Tp * (dh / 8);
     split_heads<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const __half *>(qkv), ld, B, T, Tp, H, dh,
                                                      static_cast<__half *>(Q), static_cast<__half *>(K),
