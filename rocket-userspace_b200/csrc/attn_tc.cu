@@ -35,6 +35,7 @@
 #include <stdio.h>
 #include <mutex>
 
+#define RKB_SPIN_TRIES 4096   // per-block hand-offs: see rkb_ptx.cuh
 #include "rkb_ptx.cuh"
 #include "rkb_tmap.h"
 #include "../src/rkb_kernels.h"
@@ -347,6 +348,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         tc_fence_before();
     }
 
+    __syncwarp();   // reconverge role-divergent lanes: the barrier below is warp-aligned
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();

@@ -352,6 +352,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
         tc_fence_before();
     }
 
+    __syncwarp();   // reconverge role-divergent lanes: the barrier below is warp-aligned
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();

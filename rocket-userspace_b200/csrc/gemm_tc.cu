@@ -414,6 +414,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
 
     tc_fence_before();
+    __syncwarp();   // reconverge role-divergent lanes: the barrier below is warp-aligned
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
@@ -835,6 +836,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
     }
 
     tc_fence_before();
+    __syncwarp();   // reconverge role-divergent lanes: the barrier below is warp-aligned
     cluster_sync();
     if (warp == 1) {
         tc_fence_after();

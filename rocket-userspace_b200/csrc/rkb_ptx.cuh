@@ -83,10 +83,34 @@ RKB_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
     return ok != 0;
 }
+// Non-blocking test: never suspends the thread.
+RKB_DEV bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// Non-blocking tries before the blocking wait.  0 by default: spinning warps
+// take issue slots from the warps doing work, which cost the GEMMs 3-5 %.  The
+// attention kernel, whose roles hand off every 128-key block, sets 4096 (its
+// block rate rose ~20 %).
+#ifndef RKB_SPIN_TRIES
+#define RKB_SPIN_TRIES 0
+#endif
+
 // Bounded wait for the phase of parity `parity` to complete.  Returns false if
 // the wait expired (error recorded) or another role already recorded an error.
+// The first RKB_SPIN_TRIES tries use the non-blocking test, so a phase that
+// completes within several microseconds is seen at once (a blocking try_wait
+// that finds the phase incomplete may suspend the thread for a hardware-chosen
+// time); then try_wait, which takes no issue slots while suspended.
 RKB_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int *err, int code) {
-    if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < RKB_SPIN_TRIES; ++i)
+        if (mbar_test_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;

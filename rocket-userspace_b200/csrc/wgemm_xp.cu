@@ -364,6 +364,7 @@ wgemm_xp_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
     }
 
     tc_fence_before();
+    __syncwarp();   // reconverge role-divergent lanes: the barrier below is warp-aligned
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
