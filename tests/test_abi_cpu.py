@@ -125,3 +125,41 @@ def test_log_callback_and_level(rkb):
     finally:
         rkb.lib.rocket_log_set_callback(None, None)
         rkb.lib.rocket_log_set_level(2)
+
+
+@pytest.mark.parametrize("group,kt", [(32, 32), (96, 96), (576, 576), (1024, 1024), (1440, 480),
+                                      (2880, 960), (2048, 1024)])
+def test_plan_int8_gw_kt_is_exact_partial_length(rkb, group, kt):
+    """Kt of the group-wise plan is the K per exact integer partial of the
+    precise kernel: the group, or for an int8 group wider than 1024 the widest
+    piece of at most 1024 that divides it (|a w| <= 2^14 keeps the piece's sum
+    within fp32's exact integer range)."""
+    Mt, Kt, Nt = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    K = group * 2 if group < 2880 else 2880
+    rc = rkb.lib.rocket_matmul_plan_int8_gw(128, K, 256, group, ctypes.byref(Mt), ctypes.byref(Kt),
+                                            ctypes.byref(Nt))
+    assert rc > 0
+    assert Kt.value == kt
+
+
+def test_hw_profile_layout(rkb):
+    """rocket_hw_current() follows the reference's struct layout
+    (include/rocket_hw_profile.h): the gates read max_tile from it."""
+    class Prof(ctypes.Structure):
+        _fields_ = [("name", ctypes.c_char_p), ("cbuf_banks", ctypes.c_int), ("cbuf_bank_size", ctypes.c_int),
+                    ("max_tile", ctypes.c_int), ("kgroup_2b", ctypes.c_int), ("kgroup_4b", ctypes.c_int),
+                    ("ngroup", ctypes.c_int), ("dtype_supported", ctypes.c_uint32),
+                    ("select_warning", ctypes.c_char_p), ("default_workers", ctypes.c_int)]
+    p = ctypes.cast(rkb.lib.rocket_hw_current(), ctypes.POINTER(Prof)).contents
+    assert p.name == b"b200" and p.max_tile == 256 and p.default_workers == 1
+    assert rkb.lib.rocket_hw_by_name(b"b200") == rkb.lib.rocket_hw_current()
+    assert not rkb.lib.rocket_hw_by_name(b"rk3588")
+
+
+def test_gw_mode_knob(rkb):
+    assert rkb.lib.rocket_b200_gw_mode(1) == 0
+    assert rkb.lib.rocket_b200_gw_mode(0) == 0
+    assert rkb.lib.rocket_b200_gw_mode(-1) == rkb.ROCKET_E_SHAPE
+    assert rkb.lib.rocket_activation_name(5) == b"gelu"
+    assert rkb.lib.rocket_activation_name(18) == b"log"
+    assert rkb.lib.rocket_activation_name(-1) == b"?"
