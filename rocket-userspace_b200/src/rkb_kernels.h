@@ -68,12 +68,11 @@ typedef struct {
     const void *Ws;           /* tiled fp16 scales */
     void *C; long ldc; int out_kind;
     const float *row_scale;
-    /* exact-partial (precise) group-wise form only, rkb_wgemm_xp_run:
-     * A holds the unscaled int8 values as fp16, Ws is unused */
+    /* exact-partial (precise) group-wise form only, rkb_wgemm_xi_run:
+     * A holds the int8 activations (a_f16 == 0), Ws is unused */
     const float *b_scale;     /* fp32 [N, K/group] */
     const float *a_scale_t;   /* fp32 [K/group, M] when a_scale varies with g, else NULL */
     int group;
-    int seg;                  /* K per exact partial: rkb_wgemm_xp_segment(group, w_bits) */
 } rkb_wgemm_desc;
 
 int rkb_wgemm_run(const rkb_wgemm_desc *d, int *err_word, cudaStream_t stream);
@@ -81,12 +80,11 @@ int rkb_wgemm_run(const rkb_wgemm_desc *d, int *err_word, cudaStream_t stream);
  * rkb_wgemm_run routes a_f16 descriptors here. */
 int rkb_wgemm_ts_run(const rkb_wgemm_desc *d, int *err_word, cudaStream_t stream);
 
-/* Precise group-wise form: per-segment exact integer partials (fp16 MMA on
- * unscaled integer operands), scaled by b_scale[n,g] (x a_scale[m,g]) and
- * summed across groups in fp32 in the epilogue.  row_scale, when given, is
- * applied at the end (a_scale constant along g). */
-int rkb_wgemm_xp_run(const rkb_wgemm_desc *d, int *err_word, cudaStream_t stream);
-int rkb_wgemm_xp_segment(int group, int w_bits);
+/* Precise group-wise form on the int8 tensor cores: int8 activations as they
+ * are (a_f16 == 0, lda in bytes), one exact int32 partial per group, scaled
+ * by b_scale[n,g] (x a_scale_t[g,m]) and summed across groups in fp32.
+ * row_scale, when given, is applied at the end (a_scale constant along g). */
+int rkb_wgemm_xi_run(const rkb_wgemm_desc *d, int *err_word, cudaStream_t stream);
 /* a_scale [M, nG] -> [nG, M] */
 int rkb_scale_transpose(const float *a_scale, int M, int nG, float *dst, cudaStream_t s);
 

@@ -47,9 +47,9 @@ int rocket_matmul_plan_int8_gw(int M, int K, int N, int group, int *Mt, int *Kt,
 {
     if (!m_ok(M, 0) || K <= 0 || N <= 0 || K % 32 || N % 32 || !gw_group_ok(K, group))
         return ROCKET_E_SHAPE;
-    /* Kt = K per exact integer partial: the group, or a piece of at most 1024
-     * of a wider one (the precise group-wise kernel's segment) */
-    return plan_common(M, K, N, rkb_wgemm_xp_segment(group, 8), Mt, Kt, Nt);
+    /* Kt = K per exact integer partial of the precise kernel: the group
+     * (int32 partials are exact for any group) */
+    return plan_common(M, K, N, group, Mt, Kt, Nt);
 }
 
 /* ---- hardware profile (reference include/rocket_hw_profile.h:60-108) ----- */
@@ -124,30 +124,27 @@ static int gw_precise_on(rkb_handle *h, int M, int N, int K, int group, int w_bi
                          const void *dWq, const float *dbs, void *dC, long ldc, int out_kind)
 {
     const int nG = K / group;
-    void *af = rkb_scratch(h, RKB_SCR_AUX, (size_t)M * K * 2);
     float *sc = rkb_scratch(h, RKB_SCR_ROW, (size_t)M * (a_rows_const ? 1 : nG) * sizeof(float));
-    if (!af || !sc) return ROCKET_E_NOMEM;
+    if (!sc) return ROCKET_E_NOMEM;
     int ps = rkb_prof_begin(h);
-    int rc = rkb_prescale_a(dA, NULL, M, K, group, af, h->stream);
-    if (!rc) rc = a_rows_const ? rkb_gather_row_scale(das, M, nG, sc, h->stream)
-                               : rkb_scale_transpose(das, M, nG, sc, h->stream);
+    int rc = a_rows_const ? rkb_gather_row_scale(das, M, nG, sc, h->stream)
+                          : rkb_scale_transpose(das, M, nG, sc, h->stream);
     rkb_prof_end(h, ps, RKB_K_PRESCALE);
     if (rc) return rc;
     rkb_wgemm_desc d;
     memset(&d, 0, sizeof d);
     d.M = M; d.N = N; d.K = K;
-    d.w_bits = w_bits; d.a_f16 = 1;
-    d.A = af; d.lda = K;
+    d.w_bits = w_bits;
+    d.A = dA; d.lda = K;                    /* int8 activations as given */
     d.Wq = dWq;
     d.C = dC; d.ldc = ldc; d.out_kind = out_kind;
     d.row_scale = a_rows_const ? sc : NULL;
     d.a_scale_t = a_rows_const ? NULL : sc;
     d.b_scale = dbs;
     d.group = group;
-    d.seg = rkb_wgemm_xp_segment(group, w_bits);
-    rkb_count(0, 3);
+    rkb_count(0, 2);
     ps = rkb_prof_begin(h);
-    rc = rkb_wgemm_xp_run(&d, h->err_dev, h->stream);
+    rc = rkb_wgemm_xi_run(&d, h->err_dev, h->stream);
     rkb_prof_end(h, ps, w_bits == 4 ? RKB_K_WGEMM_W4_F16 : RKB_K_WGEMM_W8_F16);
     return rc;
 }

@@ -127,13 +127,12 @@ def test_log_callback_and_level(rkb):
         rkb.lib.rocket_log_set_level(2)
 
 
-@pytest.mark.parametrize("group,kt", [(32, 32), (96, 96), (576, 576), (1024, 1024), (1440, 480),
-                                      (2880, 960), (2048, 1024)])
+@pytest.mark.parametrize("group,kt", [(32, 32), (96, 96), (576, 576), (1024, 1024), (1440, 1440),
+                                      (2880, 2880), (2048, 2048)])
 def test_plan_int8_gw_kt_is_exact_partial_length(rkb, group, kt):
     """Kt of the group-wise plan is the K per exact integer partial of the
-    precise kernel: the group, or for an int8 group wider than 1024 the widest
-    piece of at most 1024 that divides it (|a w| <= 2^14 keeps the piece's sum
-    within fp32's exact integer range)."""
+    precise kernel: the whole group, since int32 partials are exact for any
+    group (|a w| <= 2^14)."""
     Mt, Kt, Nt = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
     K = group * 2 if group < 2880 else 2880
     rc = rkb.lib.rocket_matmul_plan_int8_gw(128, K, 256, group, ctypes.byref(Mt), ctypes.byref(Kt),

@@ -55,7 +55,7 @@ def test_int8_gate_groups(dev, orc, group):
     (4, 132, 96, 320, 32, True),         # partial 64-wide K block, M and N tails
     (4, 256, 3840, 512, 32, True),       # config-3 group and per-row activation scale
     (8, 4, 96, 32, 32, False),
-    (8, 260, 2048, 96, 2048, False),     # int8 group > 1024: exact pieces of 1024
+    (8, 260, 2048, 96, 2048, False),     # int8 group 2048: one int32 partial, converted once
     (8, 64, 3840, 256, 32, True),
 ])
 def test_precise_vs_fp64(dev, orc, bits, M, K, N, group, rowconst):
@@ -76,8 +76,8 @@ def test_precise_vs_fp64(dev, orc, bits, M, K, N, group, rowconst):
 
 def test_int8_extreme_partials_exact(dev, orc):
     """|a w| = 2^14 everywhere: a 1024-wide partial reaches 2^24, the edge of
-    fp32's exact integer range.  With one group the output IS the partial, so
-    it must equal the integer product exactly."""
+    fp32's exact integer range.  With one group and unit scales the output IS
+    the partial, so it must equal the integer product exactly."""
     M, K, N, group = 64, 1024, 64, 1024
     a = np.ones((M, 1), np.float32)
     b = np.ones((N, 1), np.float32)
@@ -93,8 +93,30 @@ def test_int8_extreme_partials_exact(dev, orc):
     assert np.array_equal(C.astype(np.int64), A.astype(np.int64) @ B.astype(np.int64).T)
 
 
-def test_int8_wide_group_pieces(dev, orc):
-    """A 2048-wide int8 group is summed as two exact 1024 pieces."""
+@pytest.mark.parametrize("bits,group", [(8, 224), (8, 256), (4, 640)])
+def test_partial_conversion_edges(dev, bits, group):
+    """Extreme codes at the group widths either side of the kernel's switch
+    between seeded partials (|P| < 2^22 read back with one subtraction) and a
+    plain int -> float conversion: int8 group 224 (|P| <= 3.67e6) vs 256
+    (4.19e6), and the widest int4 group the entry accepts (640, |P| <= 6.6e5).
+    One group and unit scales, so C must equal the integer product exactly."""
+    M, N, K = 64, 64, group
+    lo, hi = (-8, 7) if bits == 4 else (-128, 127)
+    rng = np.random.default_rng(group + bits)
+    a = np.ones((M, 1), np.float32)
+    b = np.ones((N, 1), np.float32)
+    f = dev.matmul_int4_groupwise if bits == 4 else dev.matmul_int8_groupwise
+    for A, B in ((np.full((M, K), -128, np.int8), np.full((N, K), lo, np.int8)),
+                 (np.where(rng.random((M, K)) < 0.5, -128, 127).astype(np.int8),
+                  np.where(rng.random((N, K)) < 0.5, lo, hi).astype(np.int8))):
+        C = np.zeros((M, N), np.float32)
+        assert f(M, K, N, A, B, a, b, C, group) == 0
+        assert np.array_equal(C.astype(np.int64), A.astype(np.int64) @ B.astype(np.int64).T)
+
+
+def test_int8_wide_group(dev, orc):
+    """A 2048-wide int8 group is one int32 partial (up to 2^25 in magnitude
+    here, so its conversion to fp32 rounds once, as the reference's does)."""
     M, K, N, group = 64, 4096, 64, 2048
     nG = K // group
     rng = np.random.default_rng(6)
