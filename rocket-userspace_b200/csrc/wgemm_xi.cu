@@ -14,9 +14,8 @@
 //     offset int8 bytes) into signed int8 in a 128-byte-swizzled shared tile;
 //   * tcgen05.mma kind::i8 sums one group into an int32 TMEM partial -- exact
 //     for any group (|a w| <= 2^14, so 2^17 products fit int32);
-//   * the epilogue turns each partial into fp32 (exactly: |P| < 2^24 for the
-//     groups where that matters, else the reference's own int -> float step)
-//     and accumulates b_scale[n, g] * P (times a_scale[m, g] when that varies
+//   * the epilogue converts each partial to fp32 (the reference's own
+//     int -> float step; exact below 2^24) and accumulates b_scale[n, g] * P (times a_scale[m, g] when that varies
 //     with g) in fp32 registers, in group order.
 //
 // Tiles are C^T: 128 weight rows (MMA M, one weight row per TMEM lane) x NT
@@ -95,6 +94,8 @@ RKB_DEV uint2 widen8_i4(uint32_t u) {
     return make_uint2(lo, hi);
 }
 
+constexpr int XCH = 16;                 // partial columns per tcgen05.ld in the epilogue
+
 RKB_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -105,26 +106,14 @@ RKB_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 
-// A partial buffer seeded with the bits of MAGIC_F = 1.5 * 2^23 holds, after
-// the integer MMAs of a group add P (|P| < 2^22) to it, the fp32 bits of
-// exactly MAGIC_F + P: one subtraction recovers P as a float with no
-// int -> float conversion instruction.
-constexpr uint32_t MAGIC_BITS = 0x4B400000u;
-constexpr float MAGIC_F = 12582912.0f;
-
-RKB_DEV void tmem_st16_const(uint32_t taddr, uint32_t x) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-        "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(x) : "memory");
-}
-RKB_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+RKB_DEV void tmem_ld(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld16(taddr, r); }
 
 RKB_DEV void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
                  : "memory");
 }
 
-template <int WBITS, int NT, int OUT, bool AS_COL, bool MAGIC>
+template <int WBITS, int NT, int OUT, bool AS_COL>
 __global__ void __launch_bounds__(Cfg<WBITS, NT>::NUM_THREADS, 1)
 wgemm_xi_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
     using C = Cfg<WBITS, NT>;
@@ -233,7 +222,7 @@ wgemm_xi_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
                             tc_fence_after();
                         }
                         tc_mma_i8(tmem_base + b * NT, adesc + static_cast<uint64_t>(k * 2),
-                                  bdesc + static_cast<uint64_t>(k * 2), IDESC, MAGIC || pos != 0);
+                                  bdesc + static_cast<uint64_t>(k * 2), IDESC, pos != 0);
                         if (pos == grp_steps - 1) {
                             tc_commit(p_full(b));
                             ++s;
@@ -302,15 +291,8 @@ wgemm_xi_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
         const int q = warp & 3, j = e >> 2;
         const uint32_t tl = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + j * 64;
         const int nseg = g.K / g.group;
-        // every partial buffer starts free (the MMA's first wait on each
-        // completes on this arrive); with MAGIC they are seeded first
-        if (MAGIC) {
-#pragma unroll
-            for (int i = 0; i < 4 * NB; ++i) tmem_st16_const(tl + (i >> 2) * NT + (i & 3) * 16, MAGIC_BITS);
-            tmem_st_wait();
-        }
-        tc_fence_before();
-        __syncwarp();
+        // every partial buffer starts free: the MMA's first wait on each
+        // completes on this arrive
         if (lane == 0)
             for (int b = 0; b < NB; ++b) mbar_arrive(p_empty(b));
         uint32_t s = 0;
@@ -324,46 +306,44 @@ wgemm_xi_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
             float acc[64];
 #pragma unroll
             for (int c = 0; c < 64; ++c) acc[c] = 0.f;
+            // scales are loaded two groups ahead: an L2 round trip per group
+            // would otherwise sit on the epilogue's critical path
+            auto ld_bs = [&](int gi) { return (n_ok && gi < nseg) ? __ldg(bsrow + gi) : 0.f; };
+            auto ld_as = [&](int gi, int off) {
+                return (AS_COL && gi < nseg && m0 + off + lane < g.M)
+                           ? __ldg(g.a_scale_t + static_cast<size_t>(gi) * g.M + m0 + off + lane) : 0.f;
+            };
+            float bs_n1 = ld_bs(0), bs_n2 = ld_bs(1);
+            float as0_n1 = ld_as(0, 0), as1_n1 = ld_as(0, 32), as0_n2 = ld_as(1, 0), as1_n2 = ld_as(1, 32);
             for (int grp = 0; grp < nseg; ++grp, ++s) {
-                const float bs = n_ok ? __ldg(bsrow + grp) : 0.f;
-                float as0 = 0.f, as1 = 0.f;
-                if (AS_COL) {
-                    const float *ar = g.a_scale_t + static_cast<size_t>(grp) * g.M;
-                    as0 = (m0 + lane < g.M) ? __ldg(ar + m0 + lane) : 0.f;
-                    as1 = (m0 + 32 + lane < g.M) ? __ldg(ar + m0 + 32 + lane) : 0.f;
-                }
+                const float bs = bs_n1, as0 = as0_n1, as1 = as1_n1;
+                bs_n1 = bs_n2; as0_n1 = as0_n2; as1_n1 = as1_n2;
+                bs_n2 = ld_bs(grp + 2);
+                if (AS_COL) { as0_n2 = ld_as(grp + 2, 0); as1_n2 = ld_as(grp + 2, 32); }
                 const uint32_t b = s % NB;
                 if (!mbar_wait_warp(p_full(b), (s / NB) & 1, g.err, ERR_WAIT_EPILOGUE)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    uint32_t v[16];
-                    const uint32_t ta = tl + b * NT + h * 16;
-                    tmem_ld16(ta, v);
+                for (int h = 0; h < 64 / XCH; ++h) {
+                    uint32_t v[XCH];
+                    const uint32_t ta = tl + b * NT + h * XCH;
+                    tmem_ld(ta, v);
                     tmem_ld_wait();
-                    if (MAGIC) tmem_st16_const(ta, MAGIC_BITS);   // re-seed for the buffer's next group
-                    if (h == 3) {
-                        if (MAGIC) tmem_st_wait();
+                    if (h == 64 / XCH - 1) {
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(p_empty(b));
                     }
-                    float *ac = acc + h * 16;
+                    float *ac = acc + h * XCH;
                     const float2 bs2 = make_float2(bs, bs);
-                    const float asl = h < 2 ? as0 : as1;
+                    const float asl = h * XCH < 32 ? as0 : as1;
 #pragma unroll
-                    for (int c = 0; c < 16; c += 2) {
-                        float2 x;
-                        if (MAGIC) {
-                            // seed + P as float bits is exactly MAGIC_F + P
-                            x = __fadd2_rn(make_float2(__uint_as_float(v[c]), __uint_as_float(v[c + 1])),
-                                           make_float2(-MAGIC_F, -MAGIC_F));
-                        } else {
-                            x = make_float2(__int2float_rn(static_cast<int>(v[c])),
-                                            __int2float_rn(static_cast<int>(v[c + 1])));
-                        }
+                    for (int c = 0; c < XCH; c += 2) {
+                        // exact below 2^24, else rounded once as the reference's (float) cast
+                        const float2 x = make_float2(__int2float_rn(static_cast<int>(v[c])),
+                                                     __int2float_rn(static_cast<int>(v[c + 1])));
                         if (AS_COL) {
-                            const int cc = (h & 1) * 16 + c;
+                            const int cc = (h * XCH + c) & 31;
                             ac[c] = fmaf(bs * __shfl_sync(0xffffffffu, asl, cc), x.x, ac[c]);
                             ac[c + 1] = fmaf(bs * __shfl_sync(0xffffffffu, asl, cc + 1), x.y, ac[c + 1]);
                         } else {
@@ -403,14 +383,14 @@ wgemm_xi_kernel(const __grid_constant__ CUtensorMap tmB, const Args g) {
     }
 }
 
-template <int WBITS, int NT, int OUT, bool AS_COL, bool MAGIC>
+template <int WBITS, int NT, int OUT, bool AS_COL>
 int launch(const rkb_wgemm_desc *d, int *err, cudaStream_t stream) {
     using C = Cfg<WBITS, NT>;
     static std::once_flag attr_once[16];
     int dev = 0;
     cudaGetDevice(&dev);
     std::call_once(attr_once[dev & 15], [] {
-        cudaFuncSetAttribute(wgemm_xi_kernel<WBITS, NT, OUT, AS_COL, MAGIC>,
+        cudaFuncSetAttribute(wgemm_xi_kernel<WBITS, NT, OUT, AS_COL>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     });
     const int sms = rkb_device_sm_count(dev);
@@ -434,7 +414,7 @@ int launch(const rkb_wgemm_desc *d, int *err, cudaStream_t stream) {
     g.err = err;
     const int tiles = g.m_tiles * g.n_tiles;
     const int grid = tiles < sms ? tiles : sms;
-    wgemm_xi_kernel<WBITS, NT, OUT, AS_COL, MAGIC><<<grid, C::NUM_THREADS, C::SMEM, stream>>>(tb, g);
+    wgemm_xi_kernel<WBITS, NT, OUT, AS_COL><<<grid, C::NUM_THREADS, C::SMEM, stream>>>(tb, g);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         fprintf(stderr, "rkb wgemm_xi launch: %s\n", cudaGetErrorString(e));
@@ -455,14 +435,9 @@ extern "C" int rkb_wgemm_xi_run(const rkb_wgemm_desc *d, int *err, cudaStream_t 
     if (d->M <= 0 || d->N <= 0 || d->K <= 0 || d->K % 32 || d->a_f16 || !d->b_scale ||
         d->group <= 0 || d->group % 32 || d->K % d->group || d->lda % 16)
         return ROCKET_E_SHAPE;
-    // seeded partials need |P| < 2^22: |a w| <= 1024 (int4) or 16384 (int8)
-    const long maxaw = d->w_bits == 4 ? 1024 : 16384;
-    const bool magic = static_cast<long>(d->group) * maxaw < (1l << 22);
-#define RKB_XI(BITS, OUT)                                                                        \
-    if (magic) return d->a_scale_t ? launch<BITS, RKB_XI_NT, OUT, true, true>(d, err, stream)    \
-                                   : launch<BITS, RKB_XI_NT, OUT, false, true>(d, err, stream);  \
-    return d->a_scale_t ? launch<BITS, RKB_XI_NT, OUT, true, false>(d, err, stream)              \
-                        : launch<BITS, RKB_XI_NT, OUT, false, false>(d, err, stream)
+#define RKB_XI(BITS, OUT)                                                          \
+    return d->a_scale_t ? launch<BITS, RKB_XI_NT, OUT, true>(d, err, stream)       \
+                        : launch<BITS, RKB_XI_NT, OUT, false>(d, err, stream)
     if (d->w_bits == 4) {
         if (d->out_kind == RKB_OUT_F32) { RKB_XI(4, RKB_OUT_F32); }
         if (d->out_kind == RKB_OUT_F16) { RKB_XI(4, RKB_OUT_F16); }

@@ -94,12 +94,11 @@ def test_int8_extreme_partials_exact(dev, orc):
 
 
 @pytest.mark.parametrize("bits,group", [(8, 224), (8, 256), (4, 640)])
-def test_partial_conversion_edges(dev, bits, group):
-    """Extreme codes at the group widths either side of the kernel's switch
-    between seeded partials (|P| < 2^22 read back with one subtraction) and a
-    plain int -> float conversion: int8 group 224 (|P| <= 3.67e6) vs 256
-    (4.19e6), and the widest int4 group the entry accepts (640, |P| <= 6.6e5).
-    One group and unit scales, so C must equal the integer product exactly."""
+def test_partial_extremes_exact(dev, bits, group):
+    """Extreme codes with one group and unit scales: C is the int32 partial
+    converted to fp32, so it must equal the integer product exactly (every
+    |P| here is at most 2^22).  int8 groups 224 and 256, and the widest int4
+    group the entry accepts (640)."""
     M, N, K = 64, 64, group
     lo, hi = (-8, 7) if bits == 4 else (-128, 127)
     rng = np.random.default_rng(group + bits)
