@@ -576,10 +576,10 @@ def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "
                            "kernel_frac_of_measured_f16": 2 * M * N * K / (kms / max(nk, 1)) / 1e9 / peaks["bf16_tflops"],
                            "per_call_kernels": {k: v for k, v in prof.items() if v[0]}}
         L.rocket_b200_gw_mode(0)
-        res3["note"] = ("precise (default): exact integer partial per 32-wide group from the fp16 MMA on unscaled "
+        res3["note"] = ("precise (default): exact int32 partial per 32-wide group from the int8 MMA on the unscaled "
                         "operands, scaled and summed in fp32 (the reference's definition, its gates' 1e-5 rms bound); "
                         "fast: w*scale rounded to fp16 in-register before the MMA (north-star 1e-2 bound). "
-                        "Peak is the fp16 dense rate")
+                        "Fractions are of the fp16 dense rate; the precise kernel runs int8 MMAs, whose peak is twice that")
         out["config3_w4a8_gw"] = res3
         L.rocket_i4_weights_free(ctx, w)
         L.rocket_i4_ctx_free(ctx)
