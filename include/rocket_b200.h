@@ -48,10 +48,12 @@ int   rocket_b200_profile_get(int idx, const char **name, uint64_t *launches, do
 /* Group-wise int4 matmul that allocates nothing.  No counterpart in the
  * reference.  For callers that may not call cudaMalloc (a runtime that owns all
  * device memory through its own arena, a fixed memory budget, or a loop that
- * must not allocate while it runs): the same computation as
- * rocket_matmul_int4_groupwise, with its device scratch (packed codes, packed
- * scales, pre-scaled activations) taken from one array compiled into the
- * library -- 32 MiB on every GPU that loads it, held until the process exits.
+ * must not allocate while it runs): rocket_matmul_int4_groupwise's inputs and
+ * output, computed in the fast group-wise form (as rocket_b200_gw_mode(1):
+ * w * b_scale rounded to fp16 before the MMA, about 3e-4 relative error), with
+ * its device scratch (packed codes, packed scales, pre-scaled activations)
+ * taken from one array compiled into the library -- 32 MiB on every GPU that
+ * loads it, held until the process exits.
  *
  *   - A, B, a_scale, b_scale and Cf must be device memory on the current CUDA
  *     device (A and Cf 16-byte aligned); nothing is copied.

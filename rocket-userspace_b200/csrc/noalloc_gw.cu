@@ -4,10 +4,12 @@
 // every byte of device memory through its own arena, a process whose memory
 // budget is fixed up front, or a host that must not allocate while it runs
 // (a real-time or safety-certified loop).  rocket_matmul_int4_groupwise needs
-// device scratch (the packed nibble codes, the packed fp16 scales and the
-// pre-scaled fp16 activations) and takes it from a per-handle pool that grows
-// with cudaMalloc.  This file offers the same computation with that scratch in
-// one fixed array compiled into the library, so nothing is allocated per call.
+// device scratch and takes it from a per-handle pool that grows with
+// cudaMalloc.  This file computes the library's fast group-wise form (the one
+// rocket_b200_gw_mode(1) selects: w * b_scale rounded to fp16 before an fp16
+// MMA, about 3e-4 relative error), whose scratch -- the packed nibble codes,
+// the packed fp16 scales and the pre-scaled fp16 activations -- sits in one
+// fixed array compiled into the library, so nothing is allocated per call.
 //
 // Cost of the array: RKB_NOALLOC_SCRATCH_BYTES (32 MiB) of device memory on
 // every GPU that loads this library, held until the process exits.

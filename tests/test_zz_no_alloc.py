@@ -3,8 +3,10 @@
 rocket_b200_matmul_int4_groupwise_noalloc serves callers that may not call
 cudaMalloc (runtimes that own all device memory, fixed memory budgets, loops
 that must not allocate): its scratch is a fixed array inside the library.  It
-must give the same result as rocket_matmul_int4_groupwise on the same device
-inputs, call after call (the array keeps the previous call's contents).
+computes the fast group-wise form (w * b_scale rounded to fp16 before the
+MMA), so it must agree with rocket_matmul_int4_groupwise and with the exact
+definition within that form's bound (1e-2 Frobenius, 2e-2 max relative), call
+after call (the array keeps the previous call's contents).
 This file is collected last so a stop-at-first-failure run has already run
 every other test.
 """
