@@ -549,7 +549,7 @@ def other_configs(rkb, torch, peaks, derived_i8_peak, which=("c1", "c2", "c3", "
         run3 = lambda: L.rocket_matmul_int4_prepacked_gw(ctx, M, K, N, Aq.data_ptr(), asc.data_ptr(),
                                                          bsc.data_ptr(), Cf.data_ptr(), w)
         res3 = {}
-        for mode, mname, fam in ((0, "precise", "wgemm_w4_f16_tcgen05"), (1, "fast", "wgemm_w4_f16_tcgen05")):
+        for mode, mname, fam in ((0, "precise", "wgemm_gw_i8_tcgen05"), (1, "fast", "wgemm_w4_f16_tcgen05")):
             L.rocket_b200_gw_mode(mode)
             for _ in range(3):
                 run3()

@@ -27,7 +27,8 @@ enum rkb_scratch_slot {
 /* Kernel families timed by the profiler (rocket_b200_profile_*). */
 enum rkb_kfam {
     RKB_K_GEMM_I8 = 0, RKB_K_GEMM_F16, RKB_K_WGEMM_W4_F16, RKB_K_WGEMM_W8_F16, RKB_K_WGEMM_W4_I8,
-    RKB_K_PACK, RKB_K_PRESCALE, RKB_K_NORM, RKB_K_SOFTMAX, RKB_K_ATTN, RKB_K_ELEMWISE, RKB_NKFAM
+    RKB_K_PACK, RKB_K_PRESCALE, RKB_K_NORM, RKB_K_SOFTMAX, RKB_K_ATTN, RKB_K_ELEMWISE,
+    RKB_K_WGEMM_GW_I8, RKB_NKFAM
 };
 #define RKB_PROF_SLOTS 4096
 

@@ -33,7 +33,7 @@ static double g_prof_ms[RKB_NKFAM];
 static const char *g_prof_name[RKB_NKFAM] = {
     "gemm_i8_tcgen05", "gemm_f16_tcgen05", "wgemm_w4_f16_tcgen05", "wgemm_w8_f16_tcgen05",
     "wgemm_w4_i8_tcgen05", "weight_pack", "act_prescale", "norm", "softmax", "attention",
-    "elementwise"};
+    "elementwise", "wgemm_gw_i8_tcgen05"};
 
 static int prof_on(void)
 {

@@ -145,7 +145,7 @@ static int gw_precise_on(rkb_handle *h, int M, int N, int K, int group, int w_bi
     rkb_count(0, 2);
     ps = rkb_prof_begin(h);
     rc = rkb_wgemm_xi_run(&d, h->err_dev, h->stream);
-    rkb_prof_end(h, ps, w_bits == 4 ? RKB_K_WGEMM_W4_F16 : RKB_K_WGEMM_W8_F16);
+    rkb_prof_end(h, ps, RKB_K_WGEMM_GW_I8);
     return rc;
 }
 
